@@ -1,0 +1,272 @@
+/*
+ * ridge_b200.h -- C ABI of the B200-native (sm_100a) ridge GEMM hot path.
+ *
+ * Plain C: fixed-width integers, plain pointers, no CUDA or torch types. A
+ * stream is passed as `void*` (a cudaStream_t; NULL = the legacy default
+ * stream). Every entry point returns an int status: 0 = RIDGE_OK, a positive
+ * value = the cudaError_t that stopped it, a negative value = one of the
+ * RIDGE_E* codes below. Launches are asynchronous on the given stream and never
+ * synchronise; the caller owns and frees every buffer.
+ *
+ * Reference interfaces each declaration replaces are cited beside it; paths are
+ * relative to the reference project root (i-nahc/ridge).
+ */
+#ifndef RIDGE_B200_H
+#define RIDGE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+
+#define RIDGE_OK 0
+#define RIDGE_EINVAL (-1)   /* invalid tile config, shape, stride or alignment */
+#define RIDGE_EDEVICE (-2)  /* a kernel recorded a device-side error (bounded wait expired) */
+#define RIDGE_ENOTSUP (-3)  /* device is not sm_100 / feature not built */
+#define RIDGE_EIO (-4)      /* file missing or unparseable */
+#define RIDGE_ERANGE (-5)   /* index out of range */
+
+/* Human-readable text for any status returned by this library. */
+const char* ridge_status_string(int status);
+
+/* ---------------------------------------------------------------- tile configs */
+
+/*
+ * One tile configuration of the GEMM family. Replaces the kernel-side half of
+ * ridge::GemmConfig (include/ridge/config.h:18-39) and the fields of
+ * ridgebench::KernelVariant (bench/kernels/gemm-mma.cuh:368-383).
+ *   BM, BN   output tile (64, 128 or 256 each)
+ *   BK       K depth of one pipeline stage (32 or 64 FP16 = one 64B/128B swizzle row)
+ *   stages   shared-memory ring depth (2..8)
+ *   warps    epilogue warps draining TMEM (4 or 8); the CTA adds one TMA
+ *            producer warp and one MMA-issuer warp
+ *   groupM   grouped-M launch order width (gemm-mma.cuh:158-178); 1 = row-major
+ *   cta_group 1 = one CTA per tile; 2 = BM=256 tile computed by a 2-CTA cluster
+ *            with cta_group::2 MMAs (each CTA holds 128 rows). 0 = default
+ *            (2 for BM=256, else 1).
+ */
+typedef struct ridge_tile_config {
+    int32_t BM, BN, BK;
+    int32_t stages;
+    int32_t warps;
+    int32_t groupM;
+    int32_t cta_group;
+} ridge_tile_config;
+
+/*
+ * Compile- and launch-time facts of one registered variant, the analogue of
+ * KernelVariant's smemBytes/threads/regsPerThread (gemm-mma.cuh:368-383).
+ */
+typedef struct ridge_variant_info {
+    ridge_tile_config cfg;
+    int32_t smem_bytes;      /* dynamic shared memory per CTA */
+    int32_t threads;         /* threads per CTA */
+    int32_t regs_per_thread; /* from the compiled kernel (cudaFuncGetAttributes); 0 if no GPU */
+    int32_t cluster_size;    /* CTAs per cluster (1 or 2) */
+    int32_t tmem_cols;       /* Tensor Memory columns allocated per CTA */
+    int32_t acc_buffers;     /* TMEM accumulators (2 = epilogue overlaps next tile) */
+    char kernel_name[96];    /* name carrying the template args, for ncu -k regex */
+} ridge_variant_info;
+
+/* Number of registered variants (replaces ridgebench::numVariants, gemm-mma.cu:121-123). */
+int ridge_num_variants(void);
+
+/* Variant i (replaces ridgebench::variant, gemm-mma.cu:125-127). RIDGE_ERANGE if out of range. */
+int ridge_variant(int index, ridge_variant_info* out);
+
+/* Prints the variant table to stdout (replaces printVariantTable, gemm-mma.cu:132-141). */
+void ridge_print_variant_table(void);
+
+/*
+ * Validates a tile config against the hardware limits (227 KB shared memory per
+ * CTA, 512 TMEM columns, supported BM/BN/BK/warps/stages). RIDGE_OK or RIDGE_EINVAL.
+ * Fills *info when non-NULL.
+ */
+int ridge_config_check(const ridge_tile_config* cfg, ridge_variant_info* info);
+
+/*
+ * Whether `cfg` can run M x N x K with the given leading dimensions. Tiles need
+ * not divide the shape (M/N/K tails are handled), but TMA needs lda and ldb to be
+ * multiples of 8 elements and ldc must be >= N. RIDGE_OK or RIDGE_EINVAL.
+ * (Replaces the caller-side divisibility skip, measure.cu:244-248.)
+ */
+int ridge_config_valid_for_shape(const ridge_tile_config* cfg, int64_t M, int64_t N, int64_t K,
+                                 int64_t lda, int64_t ldb, int64_t ldc);
+
+/* ---------------------------------------------------------------- the GEMM */
+
+/*
+ * C[M,N] = A[M,K] * B[K,N], FP16 in, FP32 accumulate, FP16 out.
+ *   A  device pointer, row-major M x K, leading dimension lda (>= K)
+ *   B  device pointer, column-major K x N (stored N x K), leading dimension ldb (>= K)
+ *   C  device pointer, row-major M x N, leading dimension ldc (>= N)
+ * A and B must be 16-byte aligned. Asynchronous on `stream`.
+ * Replaces KernelVariant::launch, cudaError_t(const half*, const half*, float*,
+ * int, int, int, cudaStream_t) (gemm-mma.cuh:382; gemm-mma.cu:19-43).
+ */
+int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                      void* stream);
+
+/* Same, addressing the variant by its table index. */
+int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,
+                              int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                              void* stream);
+
+/*
+ * Reads (and, when clear != 0, resets) the device-side error word of the
+ * current device after synchronising it. *code = 0 when no kernel timed out.
+ * Returns RIDGE_OK, or a CUDA error from the synchronisation.
+ */
+int ridge_device_error(int clear, int32_t* code);
+
+/* ---------------------------------------------------------------- the model */
+
+/*
+ * Hardware constants for the cost model (replaces ridge::HardwareModel,
+ * include/ridge/hardware.h:9-54). Fields marked [CAL] come from the sm_100a
+ * calibration microbenchmarks.
+ */
+typedef struct ridge_hw {
+    char name[64];
+    int32_t num_sms;
+    double clock_hz;
+    double umma_cycles_per_kstep;  /* [CAL] cycles of one 128x256x16 tcgen05.mma per SM */
+    double smem_bytes_per_cycle;   /* [CAL] operand bytes/cycle/SM the tensor core reads from smem */
+    double tma_bytes_per_cycle;    /* [CAL] TMA fill bytes/cycle/SM */
+    double hbm_bytes_per_sec;      /* [CAL] whole-GPU HBM bandwidth */
+    double l2_bytes_per_sec;       /* [CAL] whole-GPU L2 -> SM bandwidth */
+    double epi_bytes_per_cycle;    /* [CAL] epilogue TMEM->global bytes/cycle/SM */
+    double launch_overhead_sec;    /* [CAL] fixed per-launch cost */
+    double stages_to_hide;         /* [CAL] pipeline stages needed to hide load latency */
+    int32_t smem_bytes_per_sm;
+    int32_t tmem_cols_per_sm;
+    int32_t max_ctas_per_sm;
+    int32_t calibrated;            /* 1 when the [CAL] fields came from a calibration file */
+} ridge_hw;
+
+/* One GEMM + tile config for the model (replaces ridge::GemmConfig, config.h:18-39). */
+typedef struct ridge_gemm_config {
+    int64_t M, N, K;
+    ridge_tile_config tile;
+} ridge_gemm_config;
+
+/* Bottleneck labels (replaces ridge::Bottleneck, include/ridge/prediction.h:10). */
+enum {
+    RIDGE_BOTTLENECK_TENSOR_CORE = 0,
+    RIDGE_BOTTLENECK_SMEM = 1,
+    RIDGE_BOTTLENECK_HBM = 2,
+    RIDGE_BOTTLENECK_OCCUPANCY = 3,
+    RIDGE_BOTTLENECK_WAVES = 4,
+    RIDGE_BOTTLENECK_ENVELOPE = 5,
+    RIDGE_BOTTLENECK_DOES_NOT_FIT = 6,
+    RIDGE_BOTTLENECK_EPILOGUE = 7
+};
+
+/* Model output (replaces ridge::Prediction, prediction.h:15-49). */
+typedef struct ridge_prediction {
+    double predicted_tflops;
+    int32_t bottleneck;
+    double compute_tflops;
+    double hbm_tflops;
+    double peak_tensor_tflops;
+    double smem_efficiency;     /* t_mma / t_step: operand feed vs tensor issue */
+    double occ_factor;          /* pipeline depth vs latency */
+    double wave_efficiency;
+    double envelope_efficiency; /* steady state share, incl. exposed epilogue */
+    double arithmetic_intensity;
+    double base_intensity;
+    double l2_reuse_factor;
+    double total_tiles;
+    double tile_slots;
+    double waves_exact;
+    double k_steps;
+    double t_mma_cycles;        /* per K-block */
+    double t_smem_cycles;       /* per K-block */
+    double t_step_cycles;       /* per K-block */
+    double t_prologue_cycles;
+    double t_epilogue_cycles;   /* per tile */
+    double t_body_cycles;       /* per tile */
+    double predicted_seconds;
+    int32_t ctas_per_sm;
+} ridge_prediction;
+
+/* Label text, e.g. "TENSOR_CORE" (replaces ridge::toString, model.cpp:9-20). */
+const char* ridge_bottleneck_string(int32_t bottleneck);
+
+/* Built-in B200 datasheet placeholders (replaces HardwareModel::a100(), hardware.cpp:19-34). */
+int ridge_hw_b200(ridge_hw* out);
+
+/*
+ * Loads a calibrated model from flat JSON, all or nothing (replaces
+ * HardwareModel::loadFromJson, hardware.cpp:149-200). On failure *out is
+ * untouched and errbuf (if non-NULL) receives the reason.
+ */
+int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t errlen);
+
+/* Predicts throughput and the binding resource (replaces ridge::predict, model.h:10). */
+int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_prediction* out);
+
+/* ---------------------------------------------------------------- autotune */
+
+/* One measured candidate. */
+typedef struct ridge_tune_entry {
+    ridge_tile_config tile;
+    double predicted_tflops;
+    double measured_tflops;   /* 0 when not benchmarked or failed */
+    int32_t device;           /* device that measured it, -1 if none */
+    int32_t status;           /* RIDGE_OK or the launch error */
+} ridge_tune_entry;
+
+/* Per-shape autotune result. */
+typedef struct ridge_tune_result {
+    int64_t M, N, K;
+    ridge_tile_config best;   /* fastest measured among the benchmarked candidates */
+    double best_tflops;
+    int32_t benchmarked;      /* candidates timed */
+    int32_t candidates;       /* valid candidates ranked by the model */
+} ridge_tune_result;
+
+/*
+ * Model-pruned empirical autotune (replaces tools/ridge-autotune.py:94-112,
+ * which only simulated the benchmark from a CSV): for each shape rank every
+ * valid registered variant by ridge_predict, benchmark the top k on the GPUs in
+ * `devices` (a host work queue, one worker thread per device, no collective),
+ * keep the fastest. k <= 0 benchmarks every candidate (the exhaustive sweep).
+ * `entries` (optional, capacity `entries_cap` per shape, row-major
+ * [shape][entry]) receives every candidate in model-rank order.
+ * timed_iters/warmup_iters control the per-candidate CUDA-event timing.
+ */
+int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
+                   const int32_t* devices, int32_t num_devices, const ridge_hw* hw,
+                   int32_t warmup_iters, int32_t timed_iters, ridge_tune_result* results,
+                   ridge_tune_entry* entries, int32_t entries_cap);
+
+/* ---------------------------------------------------------------- N-slab sharding */
+
+/*
+ * Rank `rank` of `nranks` computes its N-column slab of C = A * B for a GEMM
+ * split by N-column slabs of B with A replicated: B_slab points at rows
+ * [n0, n0 + n_slab) of the N x K storage of B, C_slab is M x n_slab row-major
+ * (ldc). The slab bounds come from ridge_slab_bounds. Purely local: no
+ * collective. The optional all-gather of C lives on the host side
+ * (torch.distributed / NCCL), see ridge_b200.sharded.
+ */
+int ridge_slab_bounds(int64_t N, int32_t nranks, int32_t rank, int64_t align, int64_t* n0,
+                      int64_t* n_slab);
+
+/*
+ * Gathers slab-major C (nranks slabs, each M x n_slab contiguous) into a
+ * row-major M x N matrix (ldc) on the device. Asynchronous on `stream`.
+ */
+int ridge_slabs_to_rowmajor(const void* slabs, void* C, int64_t M, int64_t N, int32_t nranks,
+                            int64_t ldc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RIDGE_B200_H */

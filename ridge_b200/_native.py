@@ -1,0 +1,141 @@
+"""ctypes binding of libridge_b200.so (the C ABI in include/ridge_b200.h).
+
+The library is loaded from ridge_b200/lib/. There is no fallback: if the
+native library is missing, importing ridge_b200 raises ImportError telling the
+user to build it (python -m ridge_b200.build).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libridge_b200.so"
+
+RIDGE_OK = 0
+RIDGE_EINVAL = -1
+RIDGE_EDEVICE = -2
+RIDGE_ENOTSUP = -3
+RIDGE_EIO = -4
+RIDGE_ERANGE = -5
+
+BOTTLENECKS = ["TENSOR_CORE", "SMEM", "HBM", "OCC", "WAVES", "ENVELOPE", "DOES_NOT_FIT",
+               "EPILOGUE"]
+
+
+class TileConfigC(C.Structure):
+    _fields_ = [("BM", C.c_int32), ("BN", C.c_int32), ("BK", C.c_int32), ("stages", C.c_int32),
+                ("warps", C.c_int32), ("groupM", C.c_int32), ("cta_group", C.c_int32)]
+
+
+class VariantInfoC(C.Structure):
+    _fields_ = [("cfg", TileConfigC), ("smem_bytes", C.c_int32), ("threads", C.c_int32),
+                ("regs_per_thread", C.c_int32), ("cluster_size", C.c_int32),
+                ("tmem_cols", C.c_int32), ("acc_buffers", C.c_int32),
+                ("kernel_name", C.c_char * 96)]
+
+
+class HwC(C.Structure):
+    _fields_ = [("name", C.c_char * 64), ("num_sms", C.c_int32), ("clock_hz", C.c_double),
+                ("umma_cycles_per_kstep", C.c_double), ("smem_bytes_per_cycle", C.c_double),
+                ("tma_bytes_per_cycle", C.c_double), ("hbm_bytes_per_sec", C.c_double),
+                ("l2_bytes_per_sec", C.c_double), ("epi_bytes_per_cycle", C.c_double),
+                ("launch_overhead_sec", C.c_double), ("stages_to_hide", C.c_double),
+                ("smem_bytes_per_sm", C.c_int32), ("tmem_cols_per_sm", C.c_int32),
+                ("max_ctas_per_sm", C.c_int32), ("calibrated", C.c_int32)]
+
+
+class GemmConfigC(C.Structure):
+    _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("tile", TileConfigC)]
+
+
+class PredictionC(C.Structure):
+    _fields_ = [("predicted_tflops", C.c_double), ("bottleneck", C.c_int32),
+                ("compute_tflops", C.c_double), ("hbm_tflops", C.c_double),
+                ("peak_tensor_tflops", C.c_double), ("smem_efficiency", C.c_double),
+                ("occ_factor", C.c_double), ("wave_efficiency", C.c_double),
+                ("envelope_efficiency", C.c_double), ("arithmetic_intensity", C.c_double),
+                ("base_intensity", C.c_double), ("l2_reuse_factor", C.c_double),
+                ("total_tiles", C.c_double), ("tile_slots", C.c_double),
+                ("waves_exact", C.c_double), ("k_steps", C.c_double),
+                ("t_mma_cycles", C.c_double), ("t_smem_cycles", C.c_double),
+                ("t_step_cycles", C.c_double), ("t_prologue_cycles", C.c_double),
+                ("t_epilogue_cycles", C.c_double), ("t_body_cycles", C.c_double),
+                ("predicted_seconds", C.c_double), ("ctas_per_sm", C.c_int32)]
+
+
+class TuneEntryC(C.Structure):
+    _fields_ = [("tile", TileConfigC), ("predicted_tflops", C.c_double),
+                ("measured_tflops", C.c_double), ("device", C.c_int32), ("status", C.c_int32)]
+
+
+class TuneResultC(C.Structure):
+    _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("best", TileConfigC),
+                ("best_tflops", C.c_double), ("benchmarked", C.c_int32),
+                ("candidates", C.c_int32)]
+
+
+# Every symbol the header declares, with its ctypes signature. The CPU test
+# suite checks that the built library exports each of these.
+_i64 = C.c_int64
+_i32 = C.c_int32
+_vp = C.c_void_p
+SIGNATURES = {
+    "ridge_status_string": (C.c_char_p, [C.c_int]),
+    "ridge_num_variants": (C.c_int, []),
+    "ridge_variant": (C.c_int, [C.c_int, C.POINTER(VariantInfoC)]),
+    "ridge_print_variant_table": (None, []),
+    "ridge_config_check": (C.c_int, [C.POINTER(TileConfigC), C.POINTER(VariantInfoC)]),
+    "ridge_config_valid_for_shape": (C.c_int, [C.POINTER(TileConfigC), _i64, _i64, _i64, _i64,
+                                              _i64, _i64]),
+    "ridge_gemm_launch": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
+                                    _i64, _i64, _i64, _vp]),
+    "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                            _i64, _i64, _vp]),
+    "ridge_device_error": (C.c_int, [C.c_int, C.POINTER(_i32)]),
+    "ridge_bottleneck_string": (C.c_char_p, [_i32]),
+    "ridge_hw_b200": (C.c_int, [C.POINTER(HwC)]),
+    "ridge_hw_load_json": (C.c_int, [C.c_char_p, C.POINTER(HwC), C.c_char_p, _i32]),
+    "ridge_predict": (C.c_int, [C.POINTER(GemmConfigC), C.POINTER(HwC), C.POINTER(PredictionC)]),
+    "ridge_autotune": (C.c_int, [C.POINTER(_i64), _i32, _i32, C.POINTER(_i32), _i32,
+                                 C.POINTER(HwC), _i32, _i32, C.POINTER(TuneResultC),
+                                 C.POINTER(TuneEntryC), _i32]),
+    "ridge_slab_bounds": (C.c_int, [_i64, _i32, _i32, _i64, C.POINTER(_i64), C.POINTER(_i64)]),
+    "ridge_slabs_to_rowmajor": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i64, _vp]),
+}
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise ImportError(
+            "ridge_b200: native library %s is missing; build it with "
+            "`python -m ridge_b200.build` (there is no non-native fallback)" % LIB_PATH)
+    lib = C.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | getattr(os, "RTLD_GLOBAL", 0))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue  # reported by exported_symbols(); calling it raises AttributeError
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def exported_symbols():
+    """Names from SIGNATURES that the loaded library actually exports."""
+    return [n for n in SIGNATURES if hasattr(lib, n)]
+
+
+class RidgeError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        msg = lib.ridge_status_string(status).decode()
+        super().__init__("%s%s (status %d)" % (what + ": " if what else "", msg, status))
+
+
+def check(status: int, what: str = "") -> None:
+    if status != RIDGE_OK:
+        raise RidgeError(status, what)

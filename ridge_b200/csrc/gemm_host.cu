@@ -1,0 +1,338 @@
+// C-ABI front end of the GEMM family: the variant table, config validation,
+// TMA tensor-map construction and the launcher (include/ridge_b200.h).
+//
+// Reference counterparts: the KernelVariant table and launchVariant in
+// bench/kernels/gemm-mma.cu:19-141. Differences by design: stages and groupM
+// are runtime values (one compiled kernel serves every depth), shapes need not
+// divide the tile, and every launch validates its arguments and returns a
+// status instead of relying on the caller to skip bad combinations.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/ridge_b200.h"
+#include "gemm_registry.h"
+#include "gemm_sm100.cuh"
+
+namespace ridge_b200 {
+
+// Per-device error word written by kernels whose bounded waits expire.
+__device__ int g_ridge_device_err = 0;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxDynSmem = 232448;   // 227 KB opt-in limit per CTA on sm_100
+constexpr int kSmemPerSm = 233472;    // 228 KB per SM
+constexpr int kSmemReservedPerCta = 1024;
+constexpr int kTmemColsPerSm = 512;
+
+const std::vector<KernelEntry>& registry() {
+    static const std::vector<KernelEntry> entries = [] {
+        std::vector<KernelEntry> v;
+        register_bm64(v);
+        register_bm128(v);
+        register_bm256(v);
+        return v;
+    }();
+    return entries;
+}
+
+struct DeviceState {
+    std::once_flag once;
+    cudaError_t init_err = cudaSuccess;
+    bool is_sm100 = false;
+    int num_sms = 0;
+    int* err_word = nullptr;
+    std::atomic<bool> smem_attr_set[256];
+};
+
+DeviceState g_dev[kMaxDevices];
+
+DeviceState* device_state(int* status) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *status = int(e);
+        return nullptr;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        *status = RIDGE_ENOTSUP;
+        return nullptr;
+    }
+    DeviceState& d = g_dev[dev];
+    std::call_once(d.once, [&] {
+        cudaDeviceProp prop{};
+        d.init_err = cudaGetDeviceProperties(&prop, dev);
+        if (d.init_err != cudaSuccess) return;
+        d.is_sm100 = prop.major == 10 && prop.minor == 0;
+        d.num_sms = prop.multiProcessorCount;
+        d.init_err = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err_word), g_ridge_device_err);
+        for (auto& f : d.smem_attr_set) f.store(false);
+    });
+    if (d.init_err != cudaSuccess) {
+        *status = int(d.init_err);
+        return nullptr;
+    }
+    if (!d.is_sm100) {
+        *status = RIDGE_ENOTSUP;
+        return nullptr;
+    }
+    *status = RIDGE_OK;
+    return &d;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// K-major FP16 operand, `rows` x `cols` (cols = K contiguous), leading
+// dimension `ld` elements, box = box_rows x BK with the swizzle equal to one
+// BK row (64B for BK=32, 128B for BK=64). Out-of-range elements read as zero.
+int make_operand_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                     int box_rows, int bk) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return RIDGE_ENOTSUP;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+    cuuint32_t box[2] = {cuuint32_t(bk), cuuint32_t(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? RIDGE_OK : RIDGE_EINVAL;
+}
+
+int default_cta_group(const ridge_tile_config& c) {
+    (void)c;
+    return 1;
+}
+
+const KernelEntry* find_entry(const ridge_tile_config& c, int* index = nullptr) {
+    const int cg = c.cta_group == 0 ? default_cta_group(c) : c.cta_group;
+    const auto& reg = registry();
+    for (size_t i = 0; i < reg.size(); ++i) {
+        const KernelEntry& e = reg[i];
+        if (e.BM == c.BM && e.BN == c.BN && e.BK == c.BK && e.warps == c.warps &&
+            e.cta_group == cg) {
+            if (index) *index = int(i);
+            return &e;
+        }
+    }
+    return nullptr;
+}
+
+int smem_for(const KernelEntry& e, int stages) { return e.fixed_smem + stages * e.stage_bytes; }
+
+int ctas_per_sm(const KernelEntry& e, int stages) {
+    const int by_smem = kSmemPerSm / (smem_for(e, stages) + kSmemReservedPerCta);
+    const int by_tmem = kTmemColsPerSm / e.tmem_cols;
+    const int by_threads = 2048 / e.threads;
+    return std::max(0, std::min(std::min(by_smem, by_tmem), by_threads));
+}
+
+// The registered table: the full BASELINE grid BM, BN in {64,128,256},
+// BK in {32,64}, stages in {2..5}, warps in {4,8}, groupM 8, minus the points
+// that overflow shared memory (valid-config filter below).
+struct TableRow {
+    ridge_tile_config cfg;
+};
+
+const std::vector<ridge_tile_config>& variant_table() {
+    static const std::vector<ridge_tile_config> table = [] {
+        std::vector<ridge_tile_config> t;
+        const int bms[] = {64, 128, 256}, bns[] = {64, 128, 256}, bks[] = {32, 64};
+        const int stages[] = {2, 3, 4, 5}, warps[] = {4, 8};
+        for (int bm : bms)
+            for (int bn : bns)
+                for (int bk : bks)
+                    for (int s : stages)
+                        for (int w : warps) {
+                            ridge_tile_config c{bm, bn, bk, s, w, 8, 0};
+                            if (ridge_config_check(&c, nullptr) == RIDGE_OK) t.push_back(c);
+                        }
+        return t;
+    }();
+    return table;
+}
+
+void fill_info(const KernelEntry& e, const ridge_tile_config& c, ridge_variant_info* info) {
+    std::memset(info, 0, sizeof(*info));
+    info->cfg = c;
+    info->cfg.cta_group = e.cta_group;
+    info->smem_bytes = smem_for(e, c.stages);
+    info->threads = e.threads;
+    info->cluster_size = e.cta_group;
+    info->tmem_cols = e.tmem_cols;
+    info->acc_buffers = e.acc_bufs;
+    std::snprintf(info->kernel_name, sizeof(info->kernel_name), "%s", e.name);
+    cudaFuncAttributes fa{};
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) == cudaSuccess && ndev > 0 &&
+        cudaFuncGetAttributes(&fa, e.func) == cudaSuccess)
+        info->regs_per_thread = fa.numRegs;
+    else
+        cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace ridge_b200
+
+using namespace ridge_b200;
+
+extern "C" {
+
+const char* ridge_status_string(int s) {
+    switch (s) {
+        case RIDGE_OK: return "ok";
+        case RIDGE_EINVAL: return "invalid tile config, shape, stride or alignment";
+        case RIDGE_EDEVICE: return "a kernel recorded a device-side error (bounded wait expired)";
+        case RIDGE_ENOTSUP: return "not supported on this device (needs sm_100)";
+        case RIDGE_EIO: return "file missing or unparseable";
+        case RIDGE_ERANGE: return "index out of range";
+        default: break;
+    }
+    if (s > 0) return cudaGetErrorString(cudaError_t(s));
+    return "unknown ridge status";
+}
+
+int ridge_config_check(const ridge_tile_config* cfg, ridge_variant_info* info) {
+    if (!cfg) return RIDGE_EINVAL;
+    const ridge_tile_config& c = *cfg;
+    if (c.stages < 2 || c.stages > kMaxStages || c.groupM < 1) return RIDGE_EINVAL;
+    const KernelEntry* e = find_entry(c);
+    if (!e) return RIDGE_EINVAL;
+    if (smem_for(*e, c.stages) > kMaxDynSmem) return RIDGE_EINVAL;
+    if (e->tmem_cols > kTmemColsPerSm) return RIDGE_EINVAL;
+    if (ctas_per_sm(*e, c.stages) < 1) return RIDGE_EINVAL;
+    if (info) fill_info(*e, c, info);
+    return RIDGE_OK;
+}
+
+int ridge_num_variants(void) { return int(variant_table().size()); }
+
+int ridge_variant(int index, ridge_variant_info* out) {
+    const auto& t = variant_table();
+    if (index < 0 || index >= int(t.size()) || !out) return RIDGE_ERANGE;
+    return ridge_config_check(&t[index], out);
+}
+
+void ridge_print_variant_table(void) {
+    std::printf("%3s %4s %4s %3s %6s %5s %5s %3s %7s %5s %5s\n", "idx", "BM", "BN", "BK", "stages",
+                "warps", "grpM", "cg", "smemB", "tmem", "accs");
+    for (int i = 0; i < ridge_num_variants(); ++i) {
+        ridge_variant_info v;
+        ridge_variant(i, &v);
+        std::printf("%3d %4d %4d %3d %6d %5d %5d %3d %7d %5d %5d\n", i, v.cfg.BM, v.cfg.BN,
+                    v.cfg.BK, v.cfg.stages, v.cfg.warps, v.cfg.groupM, v.cfg.cta_group,
+                    v.smem_bytes, v.tmem_cols, v.acc_buffers);
+    }
+}
+
+int ridge_config_valid_for_shape(const ridge_tile_config* cfg, int64_t M, int64_t N, int64_t K,
+                                 int64_t lda, int64_t ldb, int64_t ldc) {
+    if (ridge_config_check(cfg, nullptr) != RIDGE_OK) return RIDGE_EINVAL;
+    if (M < 0 || N < 0 || K < 0) return RIDGE_EINVAL;
+    if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
+        return RIDGE_EINVAL;
+    if (lda < K || ldb < K || ldc < N) return RIDGE_EINVAL;
+    if (lda % 8 != 0 || ldb % 8 != 0) return RIDGE_EINVAL;  // TMA: strides multiple of 16 B
+    if (lda < 8 || ldb < 8) return RIDGE_EINVAL;
+    return RIDGE_OK;
+}
+
+int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                      void* stream_v) {
+    int st = ridge_config_valid_for_shape(cfg, M, N, K, lda, ldb, ldc);
+    if (st != RIDGE_OK) return st;
+    if (M == 0 || N == 0) return RIDGE_OK;
+    if (!A || !B || !C) return RIDGE_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+        (reinterpret_cast<uintptr_t>(C) & 1))
+        return RIDGE_EINVAL;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    DeviceState* dev = device_state(&st);
+    if (!dev) return st;
+    if (K == 0) {
+        cudaError_t e = cudaMemset2DAsync(C, size_t(ldc) * 2, 0, size_t(N) * 2, size_t(M), stream);
+        return int(e);
+    }
+
+    int idx = -1;
+    const KernelEntry* e = find_entry(*cfg, &idx);
+    const int smem = smem_for(*e, cfg->stages);
+    if (!dev->smem_attr_set[idx].load(std::memory_order_acquire)) {
+        cudaError_t ce =
+            cudaFuncSetAttribute(e->func, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+        if (ce != cudaSuccess) return int(ce);
+        dev->smem_attr_set[idx].store(true, std::memory_order_release);
+    }
+
+    CUtensorMap tmap_a, tmap_b;
+    st = make_operand_map(&tmap_a, A, M, K, lda, e->tile_a_rows, e->BK);
+    if (st != RIDGE_OK) return st;
+    st = make_operand_map(&tmap_b, B, N, K, ldb, e->tile_b_rows, e->BK);
+    if (st != RIDGE_OK) return st;
+
+    GemmParams p;
+    p.C = static_cast<__half*>(C);
+    p.M = int(M);
+    p.N = int(N);
+    p.K = int(K);
+    p.ldc = ldc;
+    p.groupM = cfg->groupM;
+    p.stages = cfg->stages;
+    p.err = dev->err_word;
+
+    const int64_t tiles = ((M + e->BM - 1) / e->BM) * ((N + e->BN - 1) / e->BN);
+    const int64_t slots = int64_t(dev->num_sms / e->cta_group) * ctas_per_sm(*e, cfg->stages);
+    const int grid_units = int(std::min<int64_t>(tiles, std::max<int64_t>(slots, 1)));
+    cudaError_t ce = e->launch(&tmap_a, &tmap_b, &p, grid_units * e->cta_group, smem, stream);
+    return int(ce);
+}
+
+int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,
+                              int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                              void* stream) {
+    const auto& t = variant_table();
+    if (index < 0 || index >= int(t.size())) return RIDGE_ERANGE;
+    return ridge_gemm_launch(&t[index], A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+int ridge_device_error(int clear, int32_t* code) {
+    int st = RIDGE_OK;
+    DeviceState* dev = device_state(&st);
+    if (!dev) return st;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return int(e);
+    int v = 0;
+    e = cudaMemcpy(&v, dev->err_word, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return int(e);
+    if (code) *code = v;
+    if (clear && v != 0) {
+        e = cudaMemset(dev->err_word, 0, sizeof(int));
+        if (e != cudaSuccess) return int(e);
+    }
+    return RIDGE_OK;
+}
+
+}  // extern "C"

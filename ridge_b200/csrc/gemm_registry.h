@@ -1,0 +1,37 @@
+// Host-side registry of compiled GEMM kernels. Each instantiation file
+// (gemm_inst_bm*.cu) contributes one KernelEntry per (BM, BN, BK, warps,
+// cta_group) template instance; `stages` and `groupM` are runtime parameters of
+// every kernel, so they do not multiply the number of instantiations.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <vector>
+
+namespace ridge_b200 {
+
+struct GemmParams;
+
+using LaunchFn = cudaError_t (*)(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                 const GemmParams* params, int grid_ctas, int smem_bytes,
+                                 cudaStream_t stream);
+
+struct KernelEntry {
+    int BM, BN, BK, warps, cta_group;
+    int tile_a_rows;      // rows of A one CTA loads per stage (BM, or BM/2 for a 2-CTA pair)
+    int tile_b_rows;      // rows of B (N x K storage) one CTA loads per stage
+    int stage_bytes;      // shared memory per pipeline stage, per CTA
+    int fixed_smem;       // alignment slack + barriers
+    int tmem_cols;        // TMEM columns allocated per CTA
+    int acc_bufs;         // TMEM accumulators
+    int threads;
+    const void* func;     // the __global__ function, for attribute queries
+    LaunchFn launch;
+    const char* name;
+};
+
+void register_bm64(std::vector<KernelEntry>& out);
+void register_bm128(std::vector<KernelEntry>& out);
+void register_bm256(std::vector<KernelEntry>& out);
+
+}  // namespace ridge_b200

@@ -1,0 +1,83 @@
+"""GPU parity of the tcgen05 GEMM family against the FP64 CPU oracle.
+
+Inputs are the benchmark fill (LCG, U(-1,1), seed 0, A then B) unless noted.
+Acceptance: relative Frobenius error <= 1e-3 and max |dC| <= 2e-2 beyond the
+half-ulp rounding of the FP16 output (oracle.REL_FROB_TOL / MAX_ABS_EXCESS_TOL).
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+
+torch = pytest.importorskip("torch")
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+if torch.cuda.is_available():
+    import ridge_b200 as rb
+    from _gpu import assert_close, run_gemm, to_dev, to_host_bits
+    TileConfig = rb.TileConfig
+else:  # collected on CPU only to be skipped
+    TileConfig = None
+
+
+def _cfg(*a):
+    from ridge_b200 import TileConfig as T
+    return T(*a)
+
+
+# A spread of tile configs over BM, BN, BK, warps, stages (one per shape kind).
+CONFIGS = [
+    (128, 128, 32, 3, 4, 8),
+    (128, 256, 64, 4, 4, 8),
+    (128, 64, 64, 4, 8, 8),
+    (64, 128, 32, 2, 4, 1),
+    (64, 64, 64, 5, 8, 4),
+    (256, 128, 64, 3, 4, 8),
+    (256, 256, 32, 3, 8, 16),
+    (64, 256, 64, 4, 4, 2),
+]
+
+
+@pytest.fixture(scope="module")
+def shape_1024():
+    a, b = oracle.unit_inputs(1024, 1024, 1024, seed=0)
+    ref = oracle.gemm_f64(a, b)
+    return a, b, ref
+
+
+@pytest.mark.parametrize("c", CONFIGS, ids=lambda c: "x".join(map(str, c)))
+def test_config1_shape_all_kinds(c, shape_1024):
+    a, b, ref = shape_1024
+    cfg = _cfg(*c)
+    out = run_gemm(cfg, to_dev(a), to_dev(b), 1024, 1024, 1024)
+    assert_close(to_host_bits(out), ref, cfg.tag())
+
+
+# Ragged shapes: M/N/K tails in every dimension, K below one BK, single tiles.
+RAGGED = [(200, 136, 72), (1, 8, 8), (129, 257, 33), (64, 64, 16), (300, 520, 1000),
+          (17, 1000, 264)]
+
+
+@pytest.mark.parametrize("shape", RAGGED, ids=lambda s: "%dx%dx%d" % s)
+@pytest.mark.parametrize("c", [CONFIGS[0], CONFIGS[1], CONFIGS[3], CONFIGS[5]],
+                         ids=lambda c: "x".join(map(str, c)))
+def test_ragged_shapes(shape, c):
+    M, N, K = shape
+    a, b = oracle.unit_inputs(M, N, K, seed=7)
+    ref = oracle.gemm_f64(a, b)
+    cfg = _cfg(*c)
+    out = run_gemm(cfg, to_dev(a), to_dev(b), M, N, K)
+    assert_close(to_host_bits(out), ref, "%s %dx%dx%d" % (cfg.tag(), M, N, K))
+
+
+def test_every_registered_variant():
+    """The whole variant table on one shape with tails in M and N."""
+    M, N, K = 520, 392, 256
+    a, b = oracle.unit_inputs(M, N, K, seed=3)
+    ref = oracle.gemm_f64(a, b)
+    ad, bd = to_dev(a), to_dev(b)
+    for v in rb.variants():
+        out = run_gemm(v.config, ad, bd, M, N, K)
+        assert_close(to_host_bits(out), ref, v.config.tag())
