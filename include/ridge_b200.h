@@ -123,6 +123,19 @@ int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, 
  */
 int ridge_device_error(int clear, int32_t* code);
 
+/* ---------------------------------------------------------------- synthetic inputs */
+
+/*
+ * Fills n FP16 values on the device with the reference's deterministic LCG
+ * (s = s*1664525 + 1013904223; draw = ((s>>16)&0x7fff)/32767), bit-identical to
+ * the host fill fillDeterministic (bench/check-gemm.cu:139-145) it replaces.
+ * range 0: value = draw - 0.5 (the reference's U(-0.5,0.5));
+ * range 1: value = 2*draw - 1 (U(-1,1), the benchmark inputs).
+ * *state is the seed on entry and the LCG state after n draws on return, so
+ * consecutive calls continue one stream (A then B from seed 0).
+ */
+int ridge_fill_lcg(void* out_f16, int64_t n, uint32_t* state, int32_t range, void* stream);
+
 /* ---------------------------------------------------------------- the model */
 
 /*

@@ -94,6 +94,7 @@ SIGNATURES = {
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                             _i64, _i64, _vp]),
     "ridge_device_error": (C.c_int, [C.c_int, C.POINTER(_i32)]),
+    "ridge_fill_lcg": (C.c_int, [_vp, _i64, C.POINTER(C.c_uint32), _i32, _vp]),
     "ridge_bottleneck_string": (C.c_char_p, [_i32]),
     "ridge_hw_b200": (C.c_int, [C.POINTER(HwC)]),
     "ridge_hw_load_json": (C.c_int, [C.c_char_p, C.POINTER(HwC), C.c_char_p, _i32]),

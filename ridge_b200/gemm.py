@@ -146,3 +146,27 @@ def device_error(clear: bool = True) -> int:
     code = C.c_int32(0)
     check(lib.ridge_device_error(1 if clear else 0, C.byref(code)), "ridge_device_error")
     return code.value
+
+
+def fill_lcg(out, seed_state: int = 0, unit: bool = True, stream=None) -> int:
+    """Fills the fp16 CUDA tensor `out` (contiguous) with the reference's LCG
+    sequence starting from `seed_state`; returns the state after the fill so a
+    second call continues the stream (A then B)."""
+    import torch
+    if out.dtype != torch.float16 or not out.is_contiguous() or not out.is_cuda:
+        raise ValueError("fill_lcg needs a contiguous float16 CUDA tensor")
+    st = C.c_uint32(seed_state)
+    check(lib.ridge_fill_lcg(out.data_ptr(), out.numel(), C.byref(st), 1 if unit else 0,
+                             _stream_handle(stream)), "ridge_fill_lcg")
+    return st.value
+
+
+def synthetic_inputs(M: int, N: int, K: int, seed: int = 0, device=None):
+    """The benchmark operands: A (M, K) then B (N, K) drawn U(-1, 1) from one
+    LCG stream seeded `seed` (B is the N x K storage of a column-major B)."""
+    import torch
+    a = torch.empty((M, K), dtype=torch.float16, device=device or "cuda")
+    b = torch.empty((N, K), dtype=torch.float16, device=device or "cuda")
+    st = fill_lcg(a, seed)
+    fill_lcg(b, st)
+    return a, b
