@@ -140,25 +140,29 @@ int ridge_fill_lcg(void* out_f16, int64_t n, uint32_t* state, int32_t range, voi
 
 /*
  * Hardware constants for the cost model (replaces ridge::HardwareModel,
- * include/ridge/hardware.h:9-54). Fields marked [CAL] come from the sm_100a
- * calibration microbenchmarks.
+ * include/ridge/hardware.h:9-54). Fields marked [CAL] are measured by the
+ * sm_100a calibration microbenchmarks (include/ridge_b200_calibrate.h); the
+ * built-in ridge_hw_b200() holds datasheet-derived placeholders.
  */
 typedef struct ridge_hw {
     char name[64];
     int32_t num_sms;
-    double clock_hz;
-    double umma_cycles_per_kstep;  /* [CAL] cycles of one 128x256x16 tcgen05.mma per SM */
-    double smem_bytes_per_cycle;   /* [CAL] operand bytes/cycle/SM the tensor core reads from smem */
-    double tma_bytes_per_cycle;    /* [CAL] TMA fill bytes/cycle/SM */
-    double hbm_bytes_per_sec;      /* [CAL] whole-GPU HBM bandwidth */
-    double l2_bytes_per_sec;       /* [CAL] whole-GPU L2 -> SM bandwidth */
-    double epi_bytes_per_cycle;    /* [CAL] epilogue TMEM->global bytes/cycle/SM */
-    double launch_overhead_sec;    /* [CAL] fixed per-launch cost */
-    double stages_to_hide;         /* [CAL] pipeline stages needed to hide load latency */
+    double clock_hz;                 /* SM clock under load */
+    double umma_cycles_128x256;      /* [CAL] SM cycles per 128x256x16 FP16 tcgen05.mma */
+    double umma_m64_ratio;           /* [CAL] cycles of a 64xNx16 MMA / cycles of 128xNx16 */
+    double smem_bytes_per_cycle;     /* [CAL] operand bytes/cycle/SM the tensor core reads */
+    double smem_mma_overlap;         /* [CAL] 1: operand reads overlap the MMA (max); 0: in series (sum) */
+    double l2_bytes_per_sec;         /* [CAL] aggregate TMA L2 -> SM fill bandwidth */
+    double hbm_bytes_per_sec;        /* [CAL] whole-GPU HBM bandwidth */
+    double epi_bytes_per_cycle_w4;   /* [CAL] C bytes/cycle/SM drained by 4 epilogue warps */
+    double epi_bytes_per_cycle_w8;   /* [CAL] same with 8 epilogue warps */
+    double tma_latency_cycles;       /* [CAL] issue -> arrival latency of one stage load */
+    double launch_overhead_sec;      /* [CAL] fixed cost of one launch (launch + fill + drain) */
+    double l2_bytes;                 /* L2 capacity */
     int32_t smem_bytes_per_sm;
     int32_t tmem_cols_per_sm;
     int32_t max_ctas_per_sm;
-    int32_t calibrated;            /* 1 when the [CAL] fields came from a calibration file */
+    int32_t calibrated;              /* 1 when the [CAL] fields came from a calibration file */
 } ridge_hw;
 
 /* One GEMM + tile config for the model (replaces ridge::GemmConfig, config.h:18-39). */
@@ -176,35 +180,41 @@ enum {
     RIDGE_BOTTLENECK_WAVES = 4,
     RIDGE_BOTTLENECK_ENVELOPE = 5,
     RIDGE_BOTTLENECK_DOES_NOT_FIT = 6,
-    RIDGE_BOTTLENECK_EPILOGUE = 7
+    RIDGE_BOTTLENECK_EPILOGUE = 7,  /* exposed TMEM -> global drain (new on B200) */
+    RIDGE_BOTTLENECK_L2 = 8         /* TMA fill from L2 (new on B200) */
 };
 
-/* Model output (replaces ridge::Prediction, prediction.h:15-49). */
+/* Model output (replaces ridge::Prediction, prediction.h:15-49). Times are
+ * SM cycles unless named _sec; efficiencies are in (0, 1]. */
 typedef struct ridge_prediction {
     double predicted_tflops;
     int32_t bottleneck;
-    double compute_tflops;
-    double hbm_tflops;
-    double peak_tensor_tflops;
-    double smem_efficiency;     /* t_mma / t_step: operand feed vs tensor issue */
-    double occ_factor;          /* pipeline depth vs latency */
-    double wave_efficiency;
-    double envelope_efficiency; /* steady state share, incl. exposed epilogue */
-    double arithmetic_intensity;
-    double base_intensity;
-    double l2_reuse_factor;
+    double compute_tflops;       /* ceiling from the on-SM pipeline after all deratings */
+    double hbm_tflops;           /* HBM roofline ceiling for the modelled DRAM traffic */
+    double peak_tensor_tflops;   /* dense tensor peak at this clock */
+    double smem_efficiency;      /* t_mma / t_step: operand feed vs tensor issue */
+    double l2_efficiency;        /* t_step / max(t_step, t_l2): TMA fill from L2 */
+    double occ_factor;           /* t_kblock / pipeline period: latency hidden by `stages` */
+    double wave_efficiency;      /* tiles / (rounds * tile slots) */
+    double envelope_efficiency;  /* steady-state share: 1 - (prologue + launch) / total */
+    double epilogue_efficiency;  /* mainloop share of the per-tile period (epilogue exposure) */
+    double arithmetic_intensity; /* FLOP per modelled DRAM byte */
+    double dram_bytes;           /* modelled DRAM traffic, grouped-M order and L2 reuse included */
     double total_tiles;
-    double tile_slots;
-    double waves_exact;
-    double k_steps;
-    double t_mma_cycles;        /* per K-block */
-    double t_smem_cycles;       /* per K-block */
-    double t_step_cycles;       /* per K-block */
-    double t_prologue_cycles;
-    double t_epilogue_cycles;   /* per tile */
-    double t_body_cycles;       /* per tile */
+    double tile_slots;           /* concurrently resident CTAs (or CTA pairs) */
+    double waves_exact;          /* total_tiles / tile_slots */
+    double k_blocks;             /* ceil(K / BK) */
+    double t_mma_cycles;         /* per K-block */
+    double t_smem_cycles;        /* per K-block */
+    double t_l2_cycles;          /* per K-block */
+    double t_step_cycles;        /* per K-block, after operand-feed overlap */
+    double t_period_cycles;      /* per K-block, after latency hiding */
+    double t_epilogue_cycles;    /* per tile */
+    double t_tile_cycles;        /* per tile, epilogue overlap included */
+    double t_prologue_cycles;    /* first-fill latency per CTA */
     double predicted_seconds;
     int32_t ctas_per_sm;
+    int32_t acc_buffers;
 } ridge_prediction;
 
 /* Label text, e.g. "TENSOR_CORE" (replaces ridge::toString, model.cpp:9-20). */
@@ -258,6 +268,17 @@ int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
                    int32_t warmup_iters, int32_t timed_iters, ridge_tune_result* results,
                    ridge_tune_entry* entries, int32_t entries_cap);
 
+/*
+ * Times one config on caller-owned device buffers with CUDA events on
+ * `stream`: `warmup` launches, a short probe, then an adaptive run of at least
+ * `iters` back-to-back launches (about 20 ms of work, at most max(400, iters)).
+ * *ms_per_launch = mean launch time. Synchronises the stream. Replaces
+ * timeTflops (bench/measure.cu:121-150).
+ */
+int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                    int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                    int32_t warmup, int32_t iters, void* stream, double* ms_per_launch);
+
 /* ---------------------------------------------------------------- N-slab sharding */
 
 /*
@@ -270,13 +291,17 @@ int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
  */
 int ridge_slab_bounds(int64_t N, int32_t nranks, int32_t rank, int64_t align, int64_t* n0,
                       int64_t* n_slab);
+/* (Slab width = ceil(N / nranks) rounded up to `align`; the last slab may be
+ * narrower or empty.) */
 
 /*
- * Gathers slab-major C (nranks slabs, each M x n_slab contiguous) into a
- * row-major M x N matrix (ldc) on the device. Asynchronous on `stream`.
+ * Re-lays out slab-major C (nranks slabs, slab r = M x slab_cols row-major,
+ * contiguous, holding C[:, r*slab_cols : (r+1)*slab_cols]) into row-major
+ * M x N C (ldc). Columns at or beyond N (padding of the last slab) are
+ * dropped. Asynchronous on `stream`.
  */
 int ridge_slabs_to_rowmajor(const void* slabs, void* C, int64_t M, int64_t N, int32_t nranks,
-                            int64_t ldc, void* stream);
+                            int64_t slab_cols, int64_t ldc, void* stream);
 
 #ifdef __cplusplus
 }

@@ -21,7 +21,7 @@ RIDGE_EIO = -4
 RIDGE_ERANGE = -5
 
 BOTTLENECKS = ["TENSOR_CORE", "SMEM", "HBM", "OCC", "WAVES", "ENVELOPE", "DOES_NOT_FIT",
-               "EPILOGUE"]
+               "EPILOGUE", "L2"]
 
 
 class TileConfigC(C.Structure):
@@ -38,31 +38,32 @@ class VariantInfoC(C.Structure):
 
 class HwC(C.Structure):
     _fields_ = [("name", C.c_char * 64), ("num_sms", C.c_int32), ("clock_hz", C.c_double),
-                ("umma_cycles_per_kstep", C.c_double), ("smem_bytes_per_cycle", C.c_double),
-                ("tma_bytes_per_cycle", C.c_double), ("hbm_bytes_per_sec", C.c_double),
-                ("l2_bytes_per_sec", C.c_double), ("epi_bytes_per_cycle", C.c_double),
-                ("launch_overhead_sec", C.c_double), ("stages_to_hide", C.c_double),
-                ("smem_bytes_per_sm", C.c_int32), ("tmem_cols_per_sm", C.c_int32),
-                ("max_ctas_per_sm", C.c_int32), ("calibrated", C.c_int32)]
+                ("umma_cycles_128x256", C.c_double), ("umma_m64_ratio", C.c_double),
+                ("smem_bytes_per_cycle", C.c_double), ("smem_mma_overlap", C.c_double),
+                ("l2_bytes_per_sec", C.c_double), ("hbm_bytes_per_sec", C.c_double),
+                ("epi_bytes_per_cycle_w4", C.c_double), ("epi_bytes_per_cycle_w8", C.c_double),
+                ("tma_latency_cycles", C.c_double), ("launch_overhead_sec", C.c_double),
+                ("l2_bytes", C.c_double), ("smem_bytes_per_sm", C.c_int32),
+                ("tmem_cols_per_sm", C.c_int32), ("max_ctas_per_sm", C.c_int32),
+                ("calibrated", C.c_int32)]
 
 
 class GemmConfigC(C.Structure):
     _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("tile", TileConfigC)]
 
 
+PREDICTION_FIELDS = [
+    "predicted_tflops", "bottleneck", "compute_tflops", "hbm_tflops", "peak_tensor_tflops",
+    "smem_efficiency", "l2_efficiency", "occ_factor", "wave_efficiency", "envelope_efficiency",
+    "epilogue_efficiency", "arithmetic_intensity", "dram_bytes", "total_tiles", "tile_slots",
+    "waves_exact", "k_blocks", "t_mma_cycles", "t_smem_cycles", "t_l2_cycles", "t_step_cycles",
+    "t_period_cycles", "t_epilogue_cycles", "t_tile_cycles", "t_prologue_cycles",
+    "predicted_seconds", "ctas_per_sm", "acc_buffers"]
+_INT_PRED = {"bottleneck", "ctas_per_sm", "acc_buffers"}
+
+
 class PredictionC(C.Structure):
-    _fields_ = [("predicted_tflops", C.c_double), ("bottleneck", C.c_int32),
-                ("compute_tflops", C.c_double), ("hbm_tflops", C.c_double),
-                ("peak_tensor_tflops", C.c_double), ("smem_efficiency", C.c_double),
-                ("occ_factor", C.c_double), ("wave_efficiency", C.c_double),
-                ("envelope_efficiency", C.c_double), ("arithmetic_intensity", C.c_double),
-                ("base_intensity", C.c_double), ("l2_reuse_factor", C.c_double),
-                ("total_tiles", C.c_double), ("tile_slots", C.c_double),
-                ("waves_exact", C.c_double), ("k_steps", C.c_double),
-                ("t_mma_cycles", C.c_double), ("t_smem_cycles", C.c_double),
-                ("t_step_cycles", C.c_double), ("t_prologue_cycles", C.c_double),
-                ("t_epilogue_cycles", C.c_double), ("t_body_cycles", C.c_double),
-                ("predicted_seconds", C.c_double), ("ctas_per_sm", C.c_int32)]
+    _fields_ = [(n, C.c_int32 if n in _INT_PRED else C.c_double) for n in PREDICTION_FIELDS]
 
 
 class TuneEntryC(C.Structure):
@@ -102,8 +103,10 @@ SIGNATURES = {
     "ridge_autotune": (C.c_int, [C.POINTER(_i64), _i32, _i32, C.POINTER(_i32), _i32,
                                  C.POINTER(HwC), _i32, _i32, C.POINTER(TuneResultC),
                                  C.POINTER(TuneEntryC), _i32]),
+    "ridge_time_gemm": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                  _i64, _i64, _i32, _i32, _vp, C.POINTER(C.c_double)]),
     "ridge_slab_bounds": (C.c_int, [_i64, _i32, _i32, _i64, C.POINTER(_i64), C.POINTER(_i64)]),
-    "ridge_slabs_to_rowmajor": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i64, _vp]),
+    "ridge_slabs_to_rowmajor": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp]),
 }
 
 

@@ -1,0 +1,202 @@
+"""Model-pruned empirical autotuning and the regret report.
+
+The model ranks, the hardware decides (reference: tools/ridge-autotune.py). For
+each shape every valid registered variant is ranked by ridge_predict, the top k
+are benchmarked on the GPUs (libridge_b200's C++ farm: one worker thread per
+device, jobs pulled from a shared queue), and the fastest measured one wins.
+
+`sweep()` with k=0 benchmarks every candidate -- the exhaustive B200 sweep --
+and writes it as CSV (the reference's measured schema, bench/measure.cu:233-234,
+extended with warps, groupM, cta_group and device). `regret()` replays top-k
+selection against such a sweep exactly as the reference does against its CSV:
+for each k, pick the best measured config among the model's top k and report
+(best - picked) / best against the exhaustive best.
+
+    python -m ridge_b200.autotune --k 10 --devices 0,1          # tune the registered sweep
+    python -m ridge_b200.autotune --exhaustive out.csv           # measure every candidate
+    python -m ridge_b200.autotune --regret data/measured/b200.csv
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import ctypes as C
+import statistics
+import sys
+import time
+from pathlib import Path
+
+from ._native import BOTTLENECKS, TuneEntryC, TuneResultC, check, lib
+from .gemm import TileConfig
+from .model import HwC, default_hw, hw_to_dict, load_hw, predict
+
+ROOT = Path(__file__).resolve().parent.parent
+REGISTERED = ROOT / "data" / "sweep" / "b200-registered.csv"
+CSV_FIELDS = ["M", "N", "K", "tag", "BM", "BN", "BK", "stages", "warps", "groupM", "cta_group",
+              "smemBytes", "threads", "tmemCols", "tflops", "pred_tflops", "pred_bottleneck",
+              "device"]
+
+
+def load_sweep(path=REGISTERED):
+    shapes = []
+    for line in Path(path).read_text().splitlines():
+        if not line.strip() or line.startswith("#"):
+            continue
+        f = line.split(",")
+        if len(f) < 4:
+            raise ValueError("%s: malformed row %r" % (path, line))
+        shapes.append((int(f[0]), int(f[1]), int(f[2]), f[3]))
+    if not shapes:
+        raise ValueError("%s has no shapes" % path)
+    return shapes
+
+
+def autotune(shapes, k=10, devices=(0,), hw: HwC | None = None, warmup=3, iters=10):
+    """Runs the farm. Returns (results, entries): per shape the best measured
+    config, and every ranked candidate (benchmarked or not) in model order."""
+    hw = hw if hw is not None else default_hw()
+    n = len(shapes)
+    mnk = (C.c_int64 * (3 * n))(*[v for s in shapes for v in s[:3]])
+    devs = (C.c_int32 * len(devices))(*devices)
+    res = (TuneResultC * n)()
+    cap = lib.ridge_num_variants()
+    ent = (TuneEntryC * (n * cap))()
+    st = lib.ridge_autotune(mnk, n, k, devs, len(devices), C.byref(hw), warmup, iters, res, ent,
+                            cap)
+    check(st, "ridge_autotune")
+    results, entries = [], []
+    for s in range(n):
+        r = res[s]
+        results.append({"M": r.M, "N": r.N, "K": r.K, "best": TileConfig.from_c(r.best),
+                        "best_tflops": r.best_tflops, "benchmarked": r.benchmarked,
+                        "candidates": r.candidates})
+        rows = []
+        for i in range(r.candidates):
+            e = ent[s * cap + i]
+            rows.append({"config": TileConfig.from_c(e.tile), "pred_tflops": e.predicted_tflops,
+                         "tflops": e.measured_tflops, "device": e.device, "status": e.status})
+        entries.append(rows)
+    return results, entries
+
+
+def write_csv(path, shapes, entries, hw: HwC, note=""):
+    from .gemm import config_info
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    with open(path, "w", newline="") as f:
+        f.write("# ridge B200 measured sweep (libridge_b200 ridge_autotune, exhaustive)\n")
+        f.write("# hw_model,%s\n" % hw.name.decode())
+        if note:
+            f.write("# %s\n" % note)
+        w = csv.writer(f)
+        w.writerow(CSV_FIELDS)
+        for shape, rows in zip(shapes, entries):
+            M, N, K, tag = shape
+            for r in rows:
+                c = r["config"]
+                info = config_info(c)
+                p = predict(M, N, K, c, hw)
+                w.writerow([M, N, K, tag, c.BM, c.BN, c.BK, c.stages, c.warps, c.groupM,
+                            info.config.cta_group, info.smem_bytes, info.threads, info.tmem_cols,
+                            "%.3f" % r["tflops"], "%.3f" % p["predicted_tflops"], p.label,
+                            r["device"]])
+
+
+def load_measured(path):
+    with open(path, newline="") as f:
+        rows = list(csv.DictReader(l for l in f if not l.startswith("#")))
+    for r in rows:
+        for k in ("M", "N", "K", "BM", "BN", "BK", "stages", "warps", "groupM", "cta_group"):
+            r[k] = int(r[k])
+        r["tflops"] = float(r["tflops"])
+        r["config"] = TileConfig(r["BM"], r["BN"], r["BK"], r["stages"], r["warps"], r["groupM"],
+                                 r["cta_group"])
+    return rows
+
+
+def regret(rows, ks=(1, 3, 5, 10, 20), hw: HwC | None = None):
+    """Top-k regret of the model against an exhaustive measured sweep.
+    Predictions are recomputed with `hw` (the current model), never read
+    from the CSV. Returns {k: (mean%, worst%, exact_hits, shapes, per-shape)}."""
+    hw = hw if hw is not None else default_hw()
+    by_shape = {}
+    for r in rows:
+        p = predict(r["M"], r["N"], r["K"], r["config"], hw)["predicted_tflops"]
+        by_shape.setdefault((r["M"], r["N"], r["K"], r["tag"]), []).append((p, r["tflops"]))
+    out = {}
+    for k in ks:
+        regrets, hits, detail = [], 0, {}
+        for key, rs in by_shape.items():
+            best = max(m for _, m in rs)
+            # stable: equal predictions keep sweep (table) order, as the farm does
+            short = sorted(rs, key=lambda x: -x[0])[:k]
+            picked = max(m for _, m in short)
+            rg = (best - picked) / best * 100.0 if best > 0 else 0.0
+            regrets.append(rg)
+            hits += picked == best
+            detail[key] = rg
+        out[k] = (statistics.mean(regrets), max(regrets), hits, len(by_shape), detail)
+    return out
+
+
+def model_error(rows, hw: HwC | None = None):
+    """Mean / median / p90 / max absolute percentage error of predicted vs
+    measured TFLOP/s over a sweep (reference: bench/validate.py:252-259)."""
+    hw = hw if hw is not None else default_hw()
+    errs = []
+    for r in rows:
+        if r["tflops"] <= 0:
+            continue
+        p = predict(r["M"], r["N"], r["K"], r["config"], hw)["predicted_tflops"]
+        errs.append(abs(p - r["tflops"]) / r["tflops"] * 100.0)
+    errs.sort()
+    return {"mape": statistics.mean(errs), "median": statistics.median(errs),
+            "p90": errs[int(0.9 * (len(errs) - 1))], "max": errs[-1], "n": len(errs)}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--sweep", default=str(REGISTERED))
+    ap.add_argument("--hw", default=None, help="calibration JSON (default data/hardware/b200.json)")
+    ap.add_argument("--devices", default="0")
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--exhaustive", default=None, help="benchmark every candidate, write CSV")
+    ap.add_argument("--regret", default=None, help="report regret against this measured CSV")
+    ap.add_argument("--ks", default="1,3,5,10,20")
+    a = ap.parse_args(argv)
+    hw = load_hw(a.hw) if a.hw else default_hw()
+    ks = [int(x) for x in a.ks.split(",")]
+    if a.regret:
+        rows = load_measured(a.regret)
+        rg = regret(rows, ks, hw)
+        err = model_error(rows, hw)
+        print("model: %s" % hw.name.decode())
+        print("MAPE %.2f%%  median %.2f%%  p90 %.2f%%  max %.2f%%  (%d configs)" % (
+            err["mape"], err["median"], err["p90"], err["max"], err["n"]))
+        print("%5s %12s %12s %10s" % ("top_k", "mean regret", "worst regret", "exact"))
+        for k in ks:
+            m, w, h, n, _ = rg[k]
+            print("%5d %11.2f%% %11.2f%% %6d/%-3d" % (k, m, w, h, n))
+        return 0
+    shapes = load_sweep(a.sweep)
+    devices = [int(x) for x in a.devices.split(",")]
+    t0 = time.time()
+    results, entries = autotune(shapes, 0 if a.exhaustive else a.k, devices, hw, a.warmup,
+                                a.iters)
+    dt = time.time() - t0
+    for r in results:
+        print("%6d x %6d x %6d  best %8.1f TFLOP/s  %s  (%d of %d benchmarked)" % (
+            r["M"], r["N"], r["K"], r["best_tflops"], r["best"].tag(), r["benchmarked"],
+            r["candidates"]))
+    print("farm: %d devices, %.1f s" % (len(devices), dt))
+    if a.exhaustive:
+        write_csv(a.exhaustive, shapes, entries, hw, note="devices %s, %.1f s" % (devices, dt))
+        print("wrote", a.exhaustive)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,253 @@
+// Model-pruned empirical autotuner and the device timer it uses.
+//
+// Reference: tools/ridge-autotune.py:94-112 ranks configs by predicted
+// throughput, keeps the top k and takes the best *measured* one -- but only by
+// looking measurements up in an existing CSV. Here the top-k loop really
+// benchmarks on the GPU, from C++, and farms the (shape, candidate) jobs over
+// any number of devices: one host worker thread per device pulls jobs from a
+// shared queue, times each candidate with CUDA events on its own stream and
+// buffers, and writes the result into its slot. No collective is involved;
+// results are gathered on the host. k <= 0 benchmarks every candidate, which is
+// the exhaustive sweep that regret is measured against.
+//
+// Timer: the reference's measure.cu:121-150 method -- warm-up launches, a short
+// probe to size the run, then an adaptive number of back-to-back launches
+// between two events.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <thread>
+#include <vector>
+
+#include "../../include/ridge_b200.h"
+
+namespace {
+
+constexpr double kTargetSeconds = 0.02;  // timed work per candidate
+constexpr int kMaxIters = 400;
+
+struct Job {
+    int shape;
+    int slot;  // index into that shape's candidate list
+};
+
+struct DeviceBuffers {
+    void* a = nullptr;
+    void* b = nullptr;
+    void* c = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+};
+
+int time_on_stream(const ridge_tile_config* cfg, const void* A, const void* B, void* Cp,
+                   int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                   int32_t warmup, int32_t min_iters, cudaStream_t s, cudaEvent_t e0,
+                   cudaEvent_t e1, double* ms_out) {
+    int st = RIDGE_OK;
+    for (int i = 0; i < std::max(1, warmup); ++i) {
+        st = ridge_gemm_launch(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, s);
+        if (st != RIDGE_OK) return st;
+    }
+    cudaError_t ce = cudaEventRecord(e0, s);
+    if (ce != cudaSuccess) return int(ce);
+    for (int i = 0; i < 3; ++i) {
+        st = ridge_gemm_launch(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, s);
+        if (st != RIDGE_OK) return st;
+    }
+    cudaEventRecord(e1, s);
+    ce = cudaEventSynchronize(e1);
+    if (ce != cudaSuccess) return int(ce);
+    float probe = 0.f;
+    cudaEventElapsedTime(&probe, e0, e1);
+    int iters = int(kTargetSeconds * 1e3 / std::max(double(probe) / 3.0, 1e-4));
+    iters = std::min(std::max(iters, std::max(1, min_iters)), std::max(kMaxIters, min_iters));
+    cudaEventRecord(e0, s);
+    for (int i = 0; i < iters; ++i) {
+        st = ridge_gemm_launch(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, s);
+        if (st != RIDGE_OK) return st;
+    }
+    cudaEventRecord(e1, s);
+    ce = cudaEventSynchronize(e1);
+    if (ce != cudaSuccess) return int(ce);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    *ms_out = double(ms) / iters;
+    return RIDGE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, void* Cp,
+                    int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                    int32_t warmup, int32_t iters, void* stream, double* ms_per_launch) {
+    if (!ms_per_launch) return RIDGE_EINVAL;
+    cudaEvent_t e0, e1;
+    cudaError_t ce = cudaEventCreate(&e0);
+    if (ce != cudaSuccess) return int(ce);
+    ce = cudaEventCreate(&e1);
+    if (ce != cudaSuccess) {
+        cudaEventDestroy(e0);
+        return int(ce);
+    }
+    const int st = time_on_stream(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, warmup, iters,
+                                  static_cast<cudaStream_t>(stream), e0, e1, ms_per_launch);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return st;
+}
+
+int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const int32_t* devices,
+                   int32_t num_devices, const ridge_hw* hw_in, int32_t warmup_iters,
+                   int32_t timed_iters, ridge_tune_result* results, ridge_tune_entry* entries,
+                   int32_t entries_cap) {
+    if (!shapes || num_shapes <= 0 || !devices || num_devices <= 0 || !results)
+        return RIDGE_EINVAL;
+    ridge_hw hw;
+    if (hw_in)
+        hw = *hw_in;
+    else
+        ridge_hw_b200(&hw);
+
+    // Rank every valid registered variant per shape by the model.
+    const int nv = ridge_num_variants();
+    std::vector<std::vector<ridge_tune_entry>> cands(num_shapes);
+    int64_t maxA = 0, maxB = 0, maxC = 0;
+    for (int s = 0; s < num_shapes; ++s) {
+        const int64_t M = shapes[3 * s], N = shapes[3 * s + 1], K = shapes[3 * s + 2];
+        if (M <= 0 || N <= 0 || K <= 0 || K % 8 != 0) return RIDGE_EINVAL;
+        maxA = std::max(maxA, M * K);
+        maxB = std::max(maxB, N * K);
+        maxC = std::max(maxC, M * N);
+        for (int i = 0; i < nv; ++i) {
+            ridge_variant_info v;
+            if (ridge_variant(i, &v) != RIDGE_OK) continue;
+            if (ridge_config_valid_for_shape(&v.cfg, M, N, K, K, K, N) != RIDGE_OK) continue;
+            ridge_gemm_config g{M, N, K, v.cfg};
+            ridge_prediction p;
+            if (ridge_predict(&g, &hw, &p) != RIDGE_OK) continue;
+            if (p.bottleneck == RIDGE_BOTTLENECK_DOES_NOT_FIT) continue;
+            ridge_tune_entry e;
+            std::memset(&e, 0, sizeof(e));
+            e.tile = v.cfg;
+            e.predicted_tflops = p.predicted_tflops;
+            e.device = -1;
+            e.status = RIDGE_ERANGE;  // "not benchmarked" until a worker fills it
+            cands[s].push_back(e);
+        }
+        // Stable sort keeps table order among equal predictions.
+        std::stable_sort(cands[s].begin(), cands[s].end(),
+                         [](const ridge_tune_entry& x, const ridge_tune_entry& y) {
+                             return x.predicted_tflops > y.predicted_tflops;
+                         });
+    }
+
+    std::vector<Job> jobs;
+    for (int s = 0; s < num_shapes; ++s) {
+        const int n = int(cands[s].size());
+        const int take = k <= 0 ? n : std::min(k, n);
+        for (int i = 0; i < take; ++i) jobs.push_back({s, i});
+    }
+    // Interleave shapes so every device sees a mix (and a slow shape does not
+    // serialise behind one worker).
+    std::stable_sort(jobs.begin(), jobs.end(),
+                     [](const Job& x, const Job& y) { return x.slot < y.slot; });
+
+    std::atomic<size_t> next{0};
+    std::atomic<int> fatal{RIDGE_OK};
+    auto worker = [&](int dev) {
+        cudaError_t ce = cudaSetDevice(dev);
+        if (ce != cudaSuccess) {
+            fatal.store(int(ce));
+            return;
+        }
+        DeviceBuffers d;
+        auto fail = [&](int code) {
+            int expect = RIDGE_OK;
+            fatal.compare_exchange_strong(expect, code);
+        };
+        if ((ce = cudaMalloc(&d.a, size_t(maxA) * 2)) != cudaSuccess ||
+            (ce = cudaMalloc(&d.b, size_t(maxB) * 2)) != cudaSuccess ||
+            (ce = cudaMalloc(&d.c, size_t(maxC) * 2)) != cudaSuccess ||
+            (ce = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking)) != cudaSuccess ||
+            (ce = cudaEventCreate(&d.e0)) != cudaSuccess ||
+            (ce = cudaEventCreate(&d.e1)) != cudaSuccess) {
+            fail(int(ce));
+        } else {
+            uint32_t state = 0;
+            int st = ridge_fill_lcg(d.a, maxA, &state, 1, d.stream);
+            if (st == RIDGE_OK) st = ridge_fill_lcg(d.b, maxB, &state, 1, d.stream);
+            if (st != RIDGE_OK) fail(st);
+            cudaStreamSynchronize(d.stream);
+            while (fatal.load() == RIDGE_OK) {
+                const size_t j = next.fetch_add(1);
+                if (j >= jobs.size()) break;
+                const Job& job = jobs[j];
+                ridge_tune_entry& e = cands[job.shape][job.slot];
+                const int64_t M = shapes[3 * job.shape], N = shapes[3 * job.shape + 1],
+                              K = shapes[3 * job.shape + 2];
+                double ms = 0;
+                const int ts = time_on_stream(&e.tile, d.a, d.b, d.c, M, N, K, K, K, N,
+                                              warmup_iters, timed_iters, d.stream, d.e0, d.e1,
+                                              &ms);
+                e.device = dev;
+                e.status = ts;
+                e.measured_tflops = ts == RIDGE_OK ? 2.0 * M * N * K / (ms * 1e-3) / 1e12 : 0.0;
+                int32_t code = 0;
+                // A launch error or a device-side timeout is sticky for this
+                // device: stop this worker, the others keep going.
+                if (ts > 0) break;
+                if (ridge_device_error(1, &code) != RIDGE_OK || code != 0) {
+                    e.status = RIDGE_EDEVICE;
+                    e.measured_tflops = 0.0;
+                    break;
+                }
+            }
+        }
+        if (d.e0) cudaEventDestroy(d.e0);
+        if (d.e1) cudaEventDestroy(d.e1);
+        if (d.stream) cudaStreamDestroy(d.stream);
+        cudaFree(d.a);
+        cudaFree(d.b);
+        cudaFree(d.c);
+    };
+    std::vector<std::thread> pool;
+    for (int i = 0; i < num_devices; ++i) pool.emplace_back(worker, devices[i]);
+    for (auto& t : pool) t.join();
+
+    for (int s = 0; s < num_shapes; ++s) {
+        ridge_tune_result& r = results[s];
+        std::memset(&r, 0, sizeof(r));
+        r.M = shapes[3 * s];
+        r.N = shapes[3 * s + 1];
+        r.K = shapes[3 * s + 2];
+        r.candidates = int32_t(cands[s].size());
+        for (const ridge_tune_entry& e : cands[s]) {
+            if (e.device >= 0) ++r.benchmarked;
+            if (e.status == RIDGE_OK && e.measured_tflops > r.best_tflops) {
+                r.best_tflops = e.measured_tflops;
+                r.best = e.tile;
+            }
+        }
+        if (entries && entries_cap > 0) {
+            const int n = std::min(entries_cap, int(cands[s].size()));
+            std::memcpy(entries + size_t(s) * entries_cap, cands[s].data(),
+                        size_t(n) * sizeof(ridge_tune_entry));
+            for (int i = n; i < entries_cap; ++i) {
+                ridge_tune_entry& e = entries[size_t(s) * entries_cap + i];
+                std::memset(&e, 0, sizeof(e));
+                e.device = -1;
+                e.status = RIDGE_ERANGE;
+            }
+        }
+    }
+    return fatal.load();
+}
+
+}  // extern "C"

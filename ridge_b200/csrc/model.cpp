@@ -1,0 +1,264 @@
+// The ridge cost model re-derived for the B200 GEMM family (ridge_predict).
+//
+// Reference: src/model.cpp:22-146 (A100, mma.sync kernel). That model times
+// one K-step of one CTA as tensor issue PLUS ldmatrix time (in series, because
+// mma.sync consumes registers ldmatrix just wrote), derates by occupancy, wave
+// quantisation and a fill/drain envelope, and caps by an HBM roofline with an
+// sqrt(ctaSlots) L2 reuse factor.
+//
+// On sm_100a the kernel is different in kind, so the terms are re-derived:
+//   * tcgen05.mma reads both operands straight from shared memory; whether the
+//     operand reads add to or overlap the MMA is a calibrated constant
+//     (hw.smem_mma_overlap: 1 = max, 0 = sum), measured by the calibration
+//     microbenchmark rather than assumed;
+//   * latency is hidden by pipeline depth (stages), not by resident warps: the
+//     per-K-block period is max(t_kblock, (L + t_kblock) / stages) for TMA
+//     latency L -- the B200 analogue of the reference's occupancy factor;
+//   * the TMA fill from L2 is its own ceiling (all 148 SMs load at once);
+//   * the persistent kernel walks ceil(tiles / slots) tiles per CTA, with the
+//     epilogue of tile i overlapping the mainloop of tile i+1 when two TMEM
+//     accumulators fit, and exposed when only one does;
+//   * the HBM ceiling uses DRAM traffic from a round-by-round walk of the
+//     grouped-M tile order (groupM now matters to the prediction, which the
+//     reference model could not express -- README.md:162 there), with panels
+//     of the previous round kept in L2 when they fit;
+//   * wave quantisation is counted over 148 SMs (74 pairs for 2-CTA tiles).
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "../../include/ridge_b200.h"
+
+namespace {
+
+struct Geometry {
+    int cg;              // CTAs per tile
+    int halves;          // MMAs per K-step along M in one CTA
+    int rows_per_cta;    // A rows one CTA holds
+    double mma_m_ratio;  // cycle multiplier of the UMMA shape
+};
+
+Geometry geometry(const ridge_tile_config& t, const ridge_hw& hw) {
+    Geometry g;
+    g.cg = t.cta_group == 2 ? 2 : 1;
+    g.halves = (g.cg == 1 && t.BM == 256) ? 2 : 1;
+    g.rows_per_cta = t.BM / g.cg;
+    g.mma_m_ratio = (g.cg == 1 && t.BM == 64) ? hw.umma_m64_ratio : 1.0;
+    return g;
+}
+
+// DRAM bytes for the grouped-M persistent walk: round r runs tiles
+// [r*slots, (r+1)*slots). Within a round, concurrently running CTAs share
+// every A row-panel and B column-panel through L2 (they sweep K together), so
+// each panel is read from DRAM at most once per round; a panel also used in
+// the previous round is still in L2 if that round's panels fit in the
+// effective L2 capacity. C is written once.
+double dram_bytes(int64_t M, int64_t N, int64_t K, int BM, int BN, int groupM, int64_t slots,
+                  double l2_bytes) {
+    const int64_t num_m = (M + BM - 1) / BM;
+    const int64_t num_n = (N + BN - 1) / BN;
+    const int64_t tiles = num_m * num_n;
+    const double a_panel = double(std::min<int64_t>(BM, M)) * K * 2.0;
+    const double b_panel = double(std::min<int64_t>(BN, N)) * K * 2.0;
+    const double c_bytes = double(M) * N * 2.0;
+    const double l2_eff = 0.75 * l2_bytes;
+    // Whole problem fits: every operand byte is read once.
+    if (double(M) * K * 2.0 + double(N) * K * 2.0 <= l2_eff)
+        return double(M) * K * 2.0 + double(N) * K * 2.0 + c_bytes;
+    std::vector<int64_t> last_a(num_m, -2), last_b(num_n, -2);
+    double total = c_bytes;
+    double prev_footprint = 0.0;
+    const int64_t per_group = int64_t(groupM) * num_n;
+    for (int64_t r = 0, t0 = 0; t0 < tiles; ++r, t0 += slots) {
+        const int64_t t1 = std::min(tiles, t0 + slots);
+        const bool prev_fits = prev_footprint <= l2_eff;
+        double footprint = 0.0;
+        for (int64_t t = t0; t < t1; ++t) {
+            const int64_t group = t / per_group;
+            const int64_t first_m = group * groupM;
+            const int64_t rows = std::min<int64_t>(num_m - first_m, groupM);
+            const int64_t in_group = t - group * per_group;
+            const int64_t tm = first_m + in_group % rows;
+            const int64_t tn = in_group / rows;
+            if (last_a[tm] != r) {
+                if (!(last_a[tm] == r - 1 && prev_fits)) total += a_panel;
+                last_a[tm] = r;
+                footprint += a_panel;
+            }
+            if (last_b[tn] != r) {
+                if (!(last_b[tn] == r - 1 && prev_fits)) total += b_panel;
+                last_b[tn] = r;
+                footprint += b_panel;
+            }
+        }
+        prev_footprint = footprint;
+    }
+    return total;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ridge_bottleneck_string(int32_t b) {
+    switch (b) {
+        case RIDGE_BOTTLENECK_TENSOR_CORE: return "TENSOR_CORE";
+        case RIDGE_BOTTLENECK_SMEM: return "SMEM";
+        case RIDGE_BOTTLENECK_HBM: return "HBM";
+        case RIDGE_BOTTLENECK_OCCUPANCY: return "OCC";
+        case RIDGE_BOTTLENECK_WAVES: return "WAVES";
+        case RIDGE_BOTTLENECK_ENVELOPE: return "ENVELOPE";
+        case RIDGE_BOTTLENECK_DOES_NOT_FIT: return "DOES_NOT_FIT";
+        case RIDGE_BOTTLENECK_EPILOGUE: return "EPILOGUE";
+        case RIDGE_BOTTLENECK_L2: return "L2";
+    }
+    return "UNKNOWN";
+}
+
+int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_prediction* out) {
+    if (!cfg || !hw || !out) return RIDGE_EINVAL;
+    ridge_prediction p;
+    std::memset(&p, 0, sizeof(p));
+    const ridge_tile_config& t = cfg->tile;
+    const int64_t M = cfg->M, N = cfg->N, K = cfg->K;
+    if (M <= 0 || N <= 0 || K <= 0 || hw->num_sms <= 0 || hw->clock_hz <= 0) return RIDGE_EINVAL;
+
+    ridge_variant_info info;
+    if (ridge_config_check(&t, &info) != RIDGE_OK) {
+        p.bottleneck = RIDGE_BOTTLENECK_DOES_NOT_FIT;
+        *out = p;
+        return RIDGE_OK;
+    }
+    ridge_tile_config tc = t;
+    tc.cta_group = info.cfg.cta_group;
+    const Geometry g = geometry(tc, *hw);
+
+    // Residency: shared memory (plus the 1 KB the driver reserves per CTA),
+    // TMEM columns and threads bound the CTAs per SM.
+    const int by_smem = hw->smem_bytes_per_sm / (info.smem_bytes + 1024);
+    const int by_tmem = hw->tmem_cols_per_sm / info.tmem_cols;
+    const int by_threads = 2048 / info.threads;
+    const int cps = std::min(std::min(by_smem, by_tmem), std::min(by_threads, hw->max_ctas_per_sm));
+    if (cps < 1) {
+        p.bottleneck = RIDGE_BOTTLENECK_DOES_NOT_FIT;
+        *out = p;
+        return RIDGE_OK;
+    }
+    p.ctas_per_sm = cps;
+    p.acc_buffers = info.acc_buffers;
+
+    // ---- one K-block (BK) of one CTA, in SM cycles
+    const double kb = std::ceil(double(K) / t.BK);
+    const double mma_per_kb = double(g.halves) * (t.BK / 16);
+    const double t_mma_one = hw->umma_cycles_128x256 * (double(t.BN) / 256.0) * g.mma_m_ratio;
+    const double t_mma = mma_per_kb * t_mma_one;
+    // Operand bytes the tensor core reads per K-block on this SM: the A rows
+    // this CTA holds, and B once per M-half (a 2-CTA pair splits B's columns).
+    const double smem_read =
+        double(g.rows_per_cta) * t.BK * 2.0 + double(g.halves) * (double(t.BN) / g.cg) * t.BK * 2.0;
+    const double t_smem = smem_read / hw->smem_bytes_per_cycle;
+    const double ov = std::min(1.0, std::max(0.0, hw->smem_mma_overlap));
+    const double t_step = ov * std::max(t_mma, t_smem) + (1.0 - ov) * (t_mma + t_smem);
+    // TMA fill from L2, with every SM loading at once.
+    const double tma_bytes = (double(g.rows_per_cta) + double(t.BN) / g.cg) * t.BK * 2.0;
+    const double l2_bpc_sm = hw->l2_bytes_per_sec / (hw->clock_hz * hw->num_sms);
+    const double t_l2 = tma_bytes / l2_bpc_sm;
+
+    // ---- residency and the persistent walk
+    const int64_t num_m = (M + t.BM - 1) / t.BM;
+    const int64_t num_n = (N + t.BN - 1) / t.BN;
+    const int64_t tiles = num_m * num_n;
+    const int64_t units_per_sm_round = int64_t(hw->num_sms / g.cg) * cps;
+    const int64_t slots = std::max<int64_t>(1, units_per_sm_round);
+    const int64_t grid_units = std::min(tiles, slots);
+    const double tiles_per_unit = std::ceil(double(tiles) / double(grid_units));
+    // CTAs actually sharing one SM (a small grid leaves SMs with fewer).
+    const double resident = std::max(1.0, double(grid_units) * g.cg / hw->num_sms);
+
+    // Shared on-SM resources (tensor core, smem port) are divided among the
+    // resident CTAs; the latency each CTA must hide is not.
+    const double t_kblock = std::max(t_step, t_l2) * resident;
+    const double t_period = std::max(t_kblock, (hw->tma_latency_cycles + t_kblock) / t.stages);
+    const double t_main = kb * t_period;
+
+    const double c_bytes_tile = double(g.rows_per_cta) * t.BN * 2.0;
+    const double epi_bpc = t.warps == 8 ? hw->epi_bytes_per_cycle_w8 : hw->epi_bytes_per_cycle_w4;
+    const double t_epi = c_bytes_tile / epi_bpc * resident;
+    double t_unit;
+    double t_tile;
+    if (info.acc_buffers >= 2) {
+        t_tile = std::max(t_main, t_epi);
+        t_unit = tiles_per_unit * t_tile + std::min(t_main, t_epi);
+    } else {
+        t_tile = t_main + t_epi;
+        t_unit = tiles_per_unit * t_tile;
+    }
+    const double t_prologue = hw->tma_latency_cycles;
+    t_unit += t_prologue;
+    const double compute_sec = t_unit / hw->clock_hz + hw->launch_overhead_sec;
+
+    // ---- HBM
+    const double dram = dram_bytes(M, N, K, t.BM, t.BN, t.groupM, grid_units, hw->l2_bytes);
+    const double hbm_sec = dram / hw->hbm_bytes_per_sec + hw->launch_overhead_sec;
+
+    const double flops = 2.0 * double(M) * double(N) * double(K);
+    const double peak_flops_per_cycle_sm = 2.0 * 128.0 * 256.0 * 16.0 / hw->umma_cycles_128x256;
+    p.peak_tensor_tflops = peak_flops_per_cycle_sm * hw->clock_hz * hw->num_sms / 1e12;
+    p.compute_tflops = flops / compute_sec / 1e12;
+    p.hbm_tflops = flops / hbm_sec / 1e12;
+    p.predicted_seconds = std::max(compute_sec, hbm_sec);
+    p.predicted_tflops = flops / p.predicted_seconds / 1e12;
+    p.dram_bytes = dram;
+    p.arithmetic_intensity = flops / dram;
+
+    p.k_blocks = kb;
+    p.t_mma_cycles = t_mma;
+    p.t_smem_cycles = t_smem;
+    p.t_l2_cycles = t_l2;
+    p.t_step_cycles = t_step;
+    p.t_period_cycles = t_period;
+    p.t_epilogue_cycles = t_epi;
+    p.t_tile_cycles = t_tile;
+    p.t_prologue_cycles = t_prologue;
+    p.total_tiles = double(tiles);
+    p.tile_slots = double(slots);
+    p.waves_exact = double(tiles) / double(slots);
+
+    p.smem_efficiency = t_mma / t_step;
+    p.l2_efficiency = t_step / std::max(t_step, t_l2);
+    p.occ_factor = t_kblock / t_period;
+    // Busy share of the machine's tile slots over the kernel: a partial last
+    // round, or a grid smaller than one round, leaves slots idle.
+    p.wave_efficiency = double(tiles) / (tiles_per_unit * double(slots));
+    p.epilogue_efficiency = t_main / t_tile;
+    const double body = tiles_per_unit * t_tile;
+    p.envelope_efficiency = body / (t_unit + hw->launch_overhead_sec * hw->clock_hz);
+
+    if (hbm_sec > compute_sec) {
+        p.bottleneck = RIDGE_BOTTLENECK_HBM;
+    } else {
+        struct F {
+            double v;
+            int label;
+        } f[] = {{p.wave_efficiency, RIDGE_BOTTLENECK_WAVES},
+                 {p.envelope_efficiency, RIDGE_BOTTLENECK_ENVELOPE},
+                 {p.epilogue_efficiency, RIDGE_BOTTLENECK_EPILOGUE},
+                 {p.smem_efficiency, RIDGE_BOTTLENECK_SMEM},
+                 {p.l2_efficiency, RIDGE_BOTTLENECK_L2},
+                 {p.occ_factor, RIDGE_BOTTLENECK_OCCUPANCY}};
+        double worst = 2.0;
+        int label = RIDGE_BOTTLENECK_TENSOR_CORE;
+        for (const F& x : f)
+            if (x.v < worst) {
+                worst = x.v;
+                label = x.label;
+            }
+        p.bottleneck = worst >= 0.95 ? RIDGE_BOTTLENECK_TENSOR_CORE : label;
+    }
+    *out = p;
+    return RIDGE_OK;
+}
+
+}  // extern "C"

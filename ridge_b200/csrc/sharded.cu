@@ -1,0 +1,99 @@
+// N-slab sharding helpers for a GEMM split across ranks by column slabs of B
+// with A replicated (each rank computes C[:, n0:n0+n_slab] = A * B_slab).
+//
+// The reference is single-GPU (README.md:154 there); this is the B200 build's
+// multi-GPU mode. The data path needs no collective: a slab is an ordinary
+// GEMM on rows [n0, n0 + n_slab) of B's N x K storage. When the caller wants
+// the full C on every rank, the slabs are all-gathered (NCCL over NVLink, from
+// the host side) into a slab-major buffer, and ridge_slabs_to_rowmajor
+// re-lays them out into row-major C.
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "../../include/ridge_b200.h"
+
+namespace {
+
+// C[i, r*slab_cols + j] = slabs[r][i][j], one thread per 8 halves (16 bytes)
+// when every row start is 16-byte aligned, else per half.
+__global__ void slabs_to_rowmajor_vec(const uint4* __restrict__ slabs, uint4* __restrict__ C,
+                                      int64_t M, int64_t N, int32_t nranks, int64_t slab_cols,
+                                      int64_t ldc) {
+    const int64_t vec_per_row = slab_cols / 8;
+    const int64_t total = int64_t(nranks) * M * vec_per_row;
+    for (int64_t v = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+         v += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = v / (M * vec_per_row);
+        const int64_t rem = v - r * M * vec_per_row;
+        const int64_t i = rem / vec_per_row;
+        const int64_t j8 = rem - i * vec_per_row;
+        const int64_t col = r * slab_cols + j8 * 8;
+        if (col >= N) continue;
+        if (col + 8 <= N) {
+            C[(i * ldc + col) / 8] = slabs[v];
+        } else {
+            const __half* src = reinterpret_cast<const __half*>(slabs + v);
+            __half* dst = reinterpret_cast<__half*>(C) + i * ldc + col;
+            for (int e = 0; e < 8 && col + e < N; ++e) dst[e] = src[e];
+        }
+    }
+}
+
+__global__ void slabs_to_rowmajor_scalar(const uint16_t* __restrict__ slabs,
+                                         uint16_t* __restrict__ C, int64_t M, int64_t N,
+                                         int32_t nranks, int64_t slab_cols, int64_t ldc) {
+    const int64_t total = int64_t(nranks) * M * slab_cols;
+    for (int64_t x = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; x < total;
+         x += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = x / (M * slab_cols);
+        const int64_t rem = x - r * M * slab_cols;
+        const int64_t i = rem / slab_cols;
+        const int64_t j = rem - i * slab_cols;
+        const int64_t col = r * slab_cols + j;
+        if (col < N) C[i * ldc + col] = slabs[x];
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int ridge_slab_bounds(int64_t N, int32_t nranks, int32_t rank, int64_t align, int64_t* n0,
+                      int64_t* n_slab) {
+    if (N < 0 || nranks <= 0 || rank < 0 || rank >= nranks || align <= 0 || !n0 || !n_slab)
+        return RIDGE_EINVAL;
+    const int64_t per = ((N + nranks - 1) / nranks + align - 1) / align * align;
+    const int64_t start = std::min<int64_t>(N, int64_t(rank) * per);
+    *n0 = start;
+    *n_slab = std::min<int64_t>(per, N - start);
+    return RIDGE_OK;
+}
+
+int ridge_slabs_to_rowmajor(const void* slabs, void* C, int64_t M, int64_t N, int32_t nranks,
+                            int64_t slab_cols, int64_t ldc, void* stream) {
+    if (M < 0 || N < 0 || nranks <= 0 || slab_cols < 0 || ldc < N) return RIDGE_EINVAL;
+    if (int64_t(nranks) * slab_cols < N) return RIDGE_EINVAL;
+    if (M == 0 || N == 0) return RIDGE_OK;
+    if (!slabs || !C) return RIDGE_EINVAL;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool vec = slab_cols % 8 == 0 && ldc % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(slabs) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(C) & 15) == 0;
+    const int block = 256;
+    const int grid = 148 * 8;
+    if (vec)
+        slabs_to_rowmajor_vec<<<grid, block, 0, s>>>(static_cast<const uint4*>(slabs),
+                                                     static_cast<uint4*>(C), M, N, nranks,
+                                                     slab_cols, ldc);
+    else
+        slabs_to_rowmajor_scalar<<<grid, block, 0, s>>>(static_cast<const uint16_t*>(slabs),
+                                                        static_cast<uint16_t*>(C), M, N, nranks,
+                                                        slab_cols, ldc);
+    return int(cudaGetLastError());
+}
+
+}  // extern "C"

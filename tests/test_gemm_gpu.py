@@ -68,7 +68,14 @@ def test_ragged_shapes(shape, c):
     a, b = oracle.unit_inputs(M, N, K, seed=7)
     ref = oracle.gemm_f64(a, b)
     cfg = _cfg(*c)
-    out = run_gemm(cfg, to_dev(a), to_dev(b), M, N, K)
+    # TMA needs 16-byte row pitches: a K that is not a multiple of 8 runs with
+    # padded leading dimensions (the pad columns hold garbage the GEMM must ignore).
+    ld = (K + 7) // 8 * 8
+    ad = torch.full((M, ld), 7.0, dtype=torch.float16, device="cuda")
+    bd = torch.full((N, ld), -3.0, dtype=torch.float16, device="cuda")
+    ad[:, :K] = to_dev(a)
+    bd[:, :K] = to_dev(b)
+    out = run_gemm(cfg, ad, bd, M, N, K)
     assert_close(to_host_bits(out), ref, "%s %dx%dx%d" % (cfg.tag(), M, N, K))
 
 

@@ -1,0 +1,93 @@
+"""CPU checks of the native library: it loads, exports every function the C
+header declares, and its host-side logic (variant table, config validation,
+argument checking) behaves -- no kernel launches."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+import ridge_b200 as rb
+from ridge_b200 import TileConfig
+from ridge_b200._native import RIDGE_EINVAL, RIDGE_OK, RIDGE_ERANGE, lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ridge_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(ridge_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function():
+    names = declared_functions()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, "declared in include/ridge_b200.h but not exported: %s" % missing
+
+
+def test_every_declared_function_has_a_python_signature():
+    from ridge_b200._native import SIGNATURES
+    assert sorted(SIGNATURES) == declared_functions()
+
+
+def test_variant_table_is_the_valid_grid():
+    """BM, BN in {64,128,256} x BK in {32,64} x stages 2..5 x warps {4,8} = 144
+    points; exactly the four whose operand ring overflows 227 KB of shared
+    memory are dropped."""
+    vs = rb.variants()
+    keys = {(v.config.BM, v.config.BN, v.config.BK, v.config.stages, v.config.warps) for v in vs}
+    assert len(vs) == len(keys) == 144 - 4 * 2
+    for bm, bn, bk, s in [(128, 256, 64, 5), (256, 128, 64, 5), (256, 256, 64, 4),
+                          (256, 256, 64, 5)]:
+        for w in (4, 8):
+            assert (bm, bn, bk, s, w) not in keys
+            assert not rb.config_ok(TileConfig(bm, bn, bk, s, w, 8))
+    for v in vs:
+        assert v.smem_bytes <= 232448
+        assert v.tmem_cols in (64, 128, 256, 512)
+        assert v.threads == (2 + v.config.warps) * 32
+        assert v.config.groupM == 8
+
+
+@pytest.mark.parametrize("bad", [
+    TileConfig(96, 128, 32, 3, 4, 8), TileConfig(128, 128, 48, 3, 4, 8),
+    TileConfig(128, 128, 32, 1, 4, 8), TileConfig(128, 128, 32, 9, 4, 8),
+    TileConfig(128, 128, 32, 3, 6, 8), TileConfig(128, 128, 32, 3, 4, 0),
+])
+def test_invalid_configs_rejected(bad):
+    assert not rb.config_ok(bad)
+
+
+def test_variant_index_range():
+    v = rb._native.VariantInfoC()
+    assert lib.ridge_variant(-1, C.byref(v)) == RIDGE_ERANGE
+    assert lib.ridge_variant(rb.num_variants(), C.byref(v)) == RIDGE_ERANGE
+
+
+def test_shape_validation():
+    cfg = TileConfig(128, 128, 32, 3, 4, 8)
+    assert rb.valid_for_shape(cfg, 100, 200, 72)            # tails are fine
+    assert not rb.valid_for_shape(cfg, 100, 200, 33)        # lda = 33: not 16-byte pitch
+    assert rb.valid_for_shape(cfg, 100, 200, 33, lda=40, ldb=40)
+    assert not rb.valid_for_shape(cfg, 100, 200, 64, ldc=199)
+    assert not rb.valid_for_shape(cfg, -1, 200, 64)
+    assert not rb.valid_for_shape(cfg, 1 << 31, 8, 8)
+
+
+def test_launch_rejects_bad_arguments_before_touching_a_device():
+    cfg = TileConfig(128, 128, 32, 3, 4, 8)
+    # invalid config / strides / alignment are refused with EINVAL
+    assert rb.launch_raw(TileConfig(96, 128, 32, 3, 4, 8), 16, 16, 16, 8, 8, 8, 8, 8, 8) == RIDGE_EINVAL
+    assert rb.launch_raw(cfg, 16, 16, 16, 8, 8, 12, 12, 12, 8) == RIDGE_EINVAL
+    assert rb.launch_raw(cfg, 8, 16, 16, 8, 8, 8, 8, 8, 8) == RIDGE_EINVAL   # A not 16-byte aligned
+    assert rb.launch_raw(cfg, 0, 16, 16, 8, 8, 8, 8, 8, 8) == RIDGE_EINVAL   # null A
+    # empty problems are a successful no-op
+    assert rb.launch_raw(cfg, 0, 0, 0, 0, 8, 8, 8, 8, 8) == RIDGE_OK
+    assert rb.launch_raw(cfg, 0, 0, 0, 8, 0, 8, 8, 8, 8) == RIDGE_OK
+
+
+def test_status_strings():
+    for s in (0, -1, -2, -3, -4, -5):
+        assert lib.ridge_status_string(s)
