@@ -41,6 +41,7 @@ const std::vector<KernelEntry>& registry() {
         register_bm64(v);
         register_bm128(v);
         register_bm256(v);
+        register_bm256_pair(v);
         return v;
     }();
     return entries;
@@ -53,6 +54,7 @@ struct DeviceState {
     int num_sms = 0;
     int* err_word = nullptr;
     std::atomic<bool> smem_attr_set[256];
+    std::atomic<int> cluster_units[256][kMaxStages + 1];  // 0 = not queried yet
 };
 
 DeviceState g_dev[kMaxDevices];
@@ -77,6 +79,8 @@ DeviceState* device_state(int* status) {
         d.num_sms = prop.multiProcessorCount;
         d.init_err = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err_word), g_ridge_device_err);
         for (auto& f : d.smem_attr_set) f.store(false);
+        for (auto& row : d.cluster_units)
+            for (auto& u : row) u.store(0);
     });
     if (d.init_err != cudaSuccess) {
         *status = int(d.init_err);
@@ -121,9 +125,26 @@ int make_operand_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t co
     return r == CUDA_SUCCESS ? RIDGE_OK : RIDGE_EINVAL;
 }
 
-int default_cta_group(const ridge_tile_config& c) {
-    (void)c;
-    return 1;
+// BM=256 tiles default to the 2-CTA pair (half the shared-memory operand
+// traffic per SM and two TMEM accumulators); cta_group 1 selects the
+// single-CTA form explicitly.
+int default_cta_group(const ridge_tile_config& c) { return c.BM == 256 ? 2 : 1; }
+
+// Row-major FP16 C (rows x cols, leading dimension ld) for the epilogue's TMA
+// stores: box = 32 columns (64 B, 64B swizzle) x box_rows rows. Stores that
+// fall outside rows/cols are clipped by the hardware.
+int make_output_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return RIDGE_ENOTSUP;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+    cuuint32_t box[2] = {32, cuuint32_t(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ptr, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? RIDGE_OK : RIDGE_EINVAL;
 }
 
 const KernelEntry* find_entry(const ridge_tile_config& c, int* index = nullptr) {
@@ -149,13 +170,10 @@ int ctas_per_sm(const KernelEntry& e, int stages) {
     return std::max(0, std::min(std::min(by_smem, by_tmem), by_threads));
 }
 
-// The registered table: the full BASELINE grid BM, BN in {64,128,256},
-// BK in {32,64}, stages in {2..5}, warps in {4,8}, groupM 8, minus the points
-// that overflow shared memory (valid-config filter below).
-struct TableRow {
-    ridge_tile_config cfg;
-};
-
+// The registered table: the full grid BM, BN in {64,128,256}, BK in {32,64},
+// stages in {2..5}, warps in {4,8}, groupM 8, minus the points that overflow
+// shared memory (valid-config filter); BM=256 appears twice, as the 2-CTA pair
+// and as the single-CTA form.
 const std::vector<ridge_tile_config>& variant_table() {
     static const std::vector<ridge_tile_config> table = [] {
         std::vector<ridge_tile_config> t;
@@ -165,10 +183,11 @@ const std::vector<ridge_tile_config>& variant_table() {
             for (int bn : bns)
                 for (int bk : bks)
                     for (int s : stages)
-                        for (int w : warps) {
-                            ridge_tile_config c{bm, bn, bk, s, w, 8, 0};
-                            if (ridge_config_check(&c, nullptr) == RIDGE_OK) t.push_back(c);
-                        }
+                        for (int w : warps)
+                            for (int cg = 1; cg <= (bm == 256 ? 2 : 1); ++cg) {
+                                ridge_tile_config c{bm, bn, bk, s, w, 8, cg};
+                                if (ridge_config_check(&c, nullptr) == RIDGE_OK) t.push_back(c);
+                            }
         return t;
     }();
     return table;
@@ -287,11 +306,20 @@ int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B
         dev->smem_attr_set[idx].store(true, std::memory_order_release);
     }
 
-    CUtensorMap tmap_a, tmap_b;
+    CUtensorMap tmap_a, tmap_b, tmap_c;
     st = make_operand_map(&tmap_a, A, M, K, lda, e->tile_a_rows, e->BK);
     if (st != RIDGE_OK) return st;
     st = make_operand_map(&tmap_b, B, N, K, ldb, e->tile_b_rows, e->BK);
     if (st != RIDGE_OK) return st;
+    // The TMA-store epilogue needs a 16-byte aligned C with a 16-byte row
+    // pitch; otherwise the kernel stores directly from registers.
+    const bool tma_store =
+        (reinterpret_cast<uintptr_t>(C) & 15) == 0 && (ldc % 8) == 0;
+    std::memset(&tmap_c, 0, sizeof(tmap_c));
+    if (tma_store) {
+        st = make_output_map(&tmap_c, C, M, N, ldc, e->epi_rows);
+        if (st != RIDGE_OK) return st;
+    }
 
     GemmParams p;
     p.C = static_cast<__half*>(C);
@@ -301,12 +329,41 @@ int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B
     p.ldc = ldc;
     p.groupM = cfg->groupM;
     p.stages = cfg->stages;
+    p.tma_store = tma_store ? 1 : 0;
     p.err = dev->err_word;
 
     const int64_t tiles = ((M + e->BM - 1) / e->BM) * ((N + e->BN - 1) / e->BN);
-    const int64_t slots = int64_t(dev->num_sms / e->cta_group) * ctas_per_sm(*e, cfg->stages);
+    int64_t slots = int64_t(dev->num_sms / e->cta_group) * ctas_per_sm(*e, cfg->stages);
+    if (e->cta_group > 1) {
+        // Co-resident clusters: pairs must sit on one TPC, so ask the runtime
+        // (once per kernel, depth and device) rather than assume SMs / 2.
+        std::atomic<int>& cached = dev->cluster_units[idx][cfg->stages];
+        int units = cached.load(std::memory_order_relaxed);
+        if (units == 0) {
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(unsigned(e->cta_group * 2), 1, 1);
+            lc.blockDim = dim3(unsigned(e->threads), 1, 1);
+            lc.dynamicSmemBytes = size_t(smem);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = unsigned(e->cta_group);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            lc.attrs = attr;
+            lc.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, e->func, &lc) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = int(slots);
+            }
+            units = n;
+            cached.store(units, std::memory_order_relaxed);
+        }
+        slots = std::min<int64_t>(slots, units);
+    }
     const int grid_units = int(std::min<int64_t>(tiles, std::max<int64_t>(slots, 1)));
-    cudaError_t ce = e->launch(&tmap_a, &tmap_b, &p, grid_units * e->cta_group, smem, stream);
+    cudaError_t ce =
+        e->launch(&tmap_a, &tmap_b, &tmap_c, &p, grid_units * e->cta_group, smem, stream);
     return int(ce);
 }
 

@@ -4,7 +4,7 @@
 
 namespace ridge_b200 {
 
-#define RIDGE_1CTA(BN, BK, W) out.push_back(make_entry_1cta<128, BN, BK, W>())
+#define RIDGE_1CTA(BN, BK, W) out.push_back(make_entry<128, BN, BK, W, 1>())
 
 void register_bm128(std::vector<KernelEntry>& out) {
     RIDGE_1CTA(64, 32, 4);

@@ -13,15 +13,16 @@ namespace ridge_b200 {
 struct GemmParams;
 
 using LaunchFn = cudaError_t (*)(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
-                                 const GemmParams* params, int grid_ctas, int smem_bytes,
-                                 cudaStream_t stream);
+                                 const CUtensorMap* tmap_c, const GemmParams* params,
+                                 int grid_ctas, int smem_bytes, cudaStream_t stream);
 
 struct KernelEntry {
     int BM, BN, BK, warps, cta_group;
     int tile_a_rows;      // rows of A one CTA loads per stage (BM, or BM/2 for a 2-CTA pair)
     int tile_b_rows;      // rows of B (N x K storage) one CTA loads per stage
+    int epi_rows;         // rows of one epilogue TMA store box
     int stage_bytes;      // shared memory per pipeline stage, per CTA
-    int fixed_smem;       // alignment slack + barriers
+    int fixed_smem;       // alignment slack + epilogue staging + barriers
     int tmem_cols;        // TMEM columns allocated per CTA
     int acc_bufs;         // TMEM accumulators
     int threads;
@@ -33,5 +34,6 @@ struct KernelEntry {
 void register_bm64(std::vector<KernelEntry>& out);
 void register_bm128(std::vector<KernelEntry>& out);
 void register_bm256(std::vector<KernelEntry>& out);
+void register_bm256_pair(std::vector<KernelEntry>& out);
 
 }  // namespace ridge_b200

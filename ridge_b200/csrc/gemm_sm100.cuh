@@ -14,23 +14,29 @@
 //   * one producer thread issues TMA bulk-tensor loads of the A and B tiles into
 //     a `stages`-deep shared-memory ring guarded by full/empty mbarriers
 //     (replaces the cp.async prologue/mainloop, gemm-mma.cuh:212-291);
-//   * one MMA thread issues tcgen05.mma (128xBNx16 or 64xBNx16, kind::f16) that
-//     read both operands straight from the 64B/128B-swizzled shared-memory
-//     tiles and accumulate FP32 into TMEM (replaces ldmatrix + mma.sync and the
-//     register accumulators);
+//   * one MMA thread issues tcgen05.mma (kind::f16) that read both operands
+//     straight from the 64B/128B-swizzled shared-memory tiles and accumulate
+//     FP32 into TMEM (replaces ldmatrix + mma.sync and register accumulators);
 //   * `warps` epilogue warps drain finished accumulators TMEM -> registers ->
-//     FP16 -> global memory while the MMA thread already fills the second TMEM
-//     accumulator with the next tile (replaces the smem-staged FP32 epilogue,
-//     gemm-mma.cuh:293-342);
-//   * the kernel is persistent: grid = min(tiles, SMs x CTAs/SM) and each CTA
-//     walks tiles blockIdx.x, blockIdx.x + gridDim.x, ... in grouped-M order.
+//     FP16 -> swizzled shared-memory staging -> TMA bulk store, while the MMA
+//     thread already fills the second TMEM accumulator with the next tile
+//     (replaces the smem-staged FP32 epilogue, gemm-mma.cuh:293-342);
+//   * the kernel is persistent: grid = min(tiles, SMs x CTAs/SM) tile units,
+//     each walking tiles u, u + units, ... in grouped-M order.
+//
+// CG = 2 is the 2-CTA variant for 256-row tiles: a cluster of two CTAs on a
+// TPC computes one 256 x BN tile with cta_group::2 MMAs (M = 256). Each CTA
+// TMA-loads its own 128 rows of A and its own half of the BN rows of B, and
+// holds the 128 x BN FP32 accumulator of its rows in its own TMEM; only the
+// leader CTA (rank 0) issues MMAs, and its commits arrive on both CTAs'
+// barriers. No load is multicast: every byte is fetched by the CTA that holds it.
 //
 // M, N and K need not be multiples of the tile: TMA zero-fills out-of-range
-// operand elements and the epilogue predicates rows and columns.
+// operand elements and clips out-of-range stores.
 //
 // Warp roles (threads = (2 + warps) * 32):
 //   warp 0        lane 0: TMA producer
-//   warp 1        TMEM allocator; lane 0: MMA issuer
+//   warp 1        TMEM allocator; lane 0: MMA issuer (leader CTA only)
 //   warps 2..     epilogue. A warp may only touch TMEM lanes 32*(warp%4) ..
 //                 +31, so 4 epilogue warps cover the 128 accumulator rows and
 //                 8 warps split the columns between two such groups.
@@ -48,22 +54,25 @@ namespace ridge_b200 {
 
 constexpr int kMaxStages = 8;
 
-template <int BM_, int BN_, int BK_, int WARPS_>
+template <int BM_, int BN_, int BK_, int WARPS_, int CG_>
 struct GemmTraits {
-    static constexpr int BM = BM_, BN = BN_, BK = BK_, kEpiWarps = WARPS_;
+    static constexpr int BM = BM_, BN = BN_, BK = BK_, kEpiWarps = WARPS_, CG = CG_;
     static_assert(BM == 64 || BM == 128 || BM == 256, "BM must be 64, 128 or 256");
     static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
     static_assert(BK == 32 || BK == 64, "BK must be 32 or 64 (one 64B or 128B swizzle row)");
     static_assert(WARPS_ == 4 || WARPS_ == 8, "epilogue warps must be 4 or 8");
+    static_assert(CG == 1 || (CG == 2 && BM == 256), "the 2-CTA variant computes 256-row tiles");
 
-    static constexpr int kUmmaM = BM == 64 ? 64 : 128;  // rows per tcgen05.mma
-    static constexpr int kMHalves = BM == 256 ? 2 : 1;  // MMAs per K-step along M
-    static constexpr int kUmmaK = 16;                    // K per tcgen05.mma (FP16)
-    static constexpr int kSwizzle = BK * 2;              // bytes per operand row
-    static constexpr int kTileABytes = BM * BK * 2;
-    static constexpr int kTileBBytes = BN * BK * 2;
+    static constexpr int kRowsA = BM / CG;                 // A rows held by one CTA
+    static constexpr int kRowsB = BN / CG;                 // B rows (N) held by one CTA
+    static constexpr int kUmmaM = CG == 2 ? 256 : (BM == 64 ? 64 : 128);
+    static constexpr int kMHalves = (CG == 1 && BM == 256) ? 2 : 1;  // MMAs per K-step along M
+    static constexpr int kUmmaK = 16;                      // K per tcgen05.mma (FP16)
+    static constexpr int kSwizzle = BK * 2;                // bytes per operand row
+    static constexpr int kTileABytes = kRowsA * BK * 2;
+    static constexpr int kTileBBytes = kRowsB * BK * 2;
     static constexpr int kStageBytes = kTileABytes + kTileBBytes;
-    static constexpr int kAccCols = BN * kMHalves;       // FP32 TMEM columns per accumulator
+    static constexpr int kAccCols = BN * kMHalves;         // FP32 TMEM columns per accumulator
     static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
     static constexpr int kTmemColsRaw = kAccCols * kAccBufs;
     static constexpr int kTmemCols = kTmemColsRaw <= 32    ? 32
@@ -72,12 +81,17 @@ struct GemmTraits {
                                      : kTmemColsRaw <= 256 ? 256
                                                            : 512;
     static constexpr int kThreads = (2 + kEpiWarps) * 32;
+    // Epilogue staging: per warp, two buffers of one 32-row x 32-column FP16
+    // chunk (rows of 64 B, 64B-swizzled) feeding TMA stores.
+    static constexpr int kEpiRowsPerWarp = BM == 64 ? 16 : 32;
+    static constexpr int kEpiChunkBytes = 32 * 64;
+    static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiChunkBytes;
     static constexpr int kBarrierBytes = 256;
     static constexpr int kAlignSlack = 1024;
     static constexpr uint32_t kIdesc = make_idesc_f16_f32(kUmmaM, BN);
 
     static constexpr int smem_bytes(int stages) {
-        return kAlignSlack + stages * kStageBytes + kBarrierBytes;
+        return kAlignSlack + stages * kStageBytes + kEpiBytes + kBarrierBytes;
     }
 };
 
@@ -87,12 +101,13 @@ struct GemmParams {
     long long ldc;
     int groupM;
     int stages;
+    int tma_store;  // 1: epilogue stores through the C tensor map; 0: direct st.global
     int* err;
 };
 
 // Grouped-M tile order, the same mapping as the reference launch order
 // (gemm-mma.cuh:158-178): tiles are taken groupM row-tiles at a time, column by
-// column inside the group, so CTAs running at the same moment share A row
+// column inside the group, so units running at the same moment share A row
 // panels and B column panels in L2.
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int groupM, int& tm,
                                             int& tn) {
@@ -105,14 +120,20 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     tn = in_group / rows;
 }
 
-template <int BM, int BN, int BK, int WARPS>
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int BM, int BN, int BK, int WARPS, int CG>
 __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     ridge_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a,
-                     const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
-    using T = GemmTraits<BM, BN, BK, WARPS>;
+                     const __grid_constant__ CUtensorMap tmap_b,
+                     const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
+    using T = GemmTraits<BM, BN, BK, WARPS, CG>;
     extern __shared__ uint8_t smem_raw[];
 
-    // 1024-byte alignment: the 128B swizzle pattern is a function of absolute
+    // 1024-byte alignment: the swizzle patterns are functions of absolute
     // shared-memory address bits, so TMA writes and UMMA descriptor reads agree
     // only when every tile starts on a 1024-byte boundary.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -120,18 +141,21 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     uint8_t* base_ptr = smem_raw + (base - raw_addr);
 
     const int stages = p.stages;
-    const uint32_t bars = base + stages * T::kStageBytes;
+    const uint32_t epi_base = base + stages * T::kStageBytes;
+    const uint32_t bars = epi_base + T::kEpiBytes;
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (kMaxStages + s); };
     auto tfull_bar = [&](int b) { return bars + 8u * (2 * kMaxStages + b); };
     auto tempty_bar = [&](int b) { return bars + 8u * (2 * kMaxStages + 2 + b); };
     const uint32_t drain_bar = bars + 8u * (2 * kMaxStages + 4);
-    uint8_t* bar_ptr = base_ptr + stages * T::kStageBytes;
+    uint8_t* bar_ptr = base_ptr + (bars - base);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 8 * (2 * kMaxStages + 5));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_cta_rank() : 0u;
+    const bool leader = rank == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -140,20 +164,25 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         }
         for (int b = 0; b < T::kAccBufs; ++b) {
             mbar_init(tfull_bar(b), 1);
-            mbar_init(tempty_bar(b), T::kEpiWarps);
+            mbar_init(tempty_bar(b), CG * T::kEpiWarps);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmap_a);
         tma_prefetch_desc(&tmap_b);
+        if (p.tma_store) tma_prefetch_desc(&tmap_c);
     }
     if (warp == 1) {
-        tmem_alloc<1>(smem_u32(tmem_slot), T::kTmemCols);
-        tmem_relinquish<1>();
+        tmem_alloc<CG>(smem_u32(tmem_slot), T::kTmemCols);
+        tmem_relinquish<CG>();
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) {
+        cluster_sync();  // both CTAs' barriers and TMEM exist before any remote use
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -161,16 +190,23 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     const int num_n = (p.N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (p.K + BK - 1) / BK;
+    const int unit = blockIdx.x / CG;
+    const int num_units = gridDim.x / CG;
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------ TMA producer
+        // In a pair, both CTAs' loads complete on the leader's full barrier,
+        // which the leader arms with the bytes of both.
+        const uint32_t leader_full0 = CG == 2 ? map_to_cta(full_bar(0), 0) : full_bar(0);
         int stage = 0;
         uint32_t phase = 0;
         long long issued = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        for (int tile = unit; tile < num_tiles && ok; tile += num_units) {
             int tm, tn;
             tile_coords(tile, num_m, num_n, p.groupM, tm, tn);
+            const int a_row = tm * BM + int(rank) * T::kRowsA;
+            const int b_row = tn * BN + int(rank) * T::kRowsB;
             for (int kb = 0; kb < num_kb; ++kb) {
                 if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err,
                                kErrTimeoutProducer)) {
@@ -178,9 +214,16 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                     break;
                 }
                 const uint32_t sa = base + stage * T::kStageBytes;
-                mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
-                tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, tm * BM);
-                tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK, tn * BN);
+                if constexpr (CG == 1) {
+                    mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
+                    tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, a_row);
+                    tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK, b_row);
+                } else {
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
+                    const uint32_t fb = leader_full0 + 8u * stage;
+                    tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, a_row);
+                    tma_load_2d_pair(sa + T::kTileABytes, &tmap_b, fb, kb * BK, b_row);
+                }
                 ++issued;
                 if (++stage == stages) {
                     stage = 0;
@@ -188,9 +231,11 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
             }
         }
-        if (!ok) {
+        if (!ok && leader) {
             // Abort path: let every load already in flight land before the CTA
-            // can exit. Issue i went to stage i % stages with parity
+            // can exit (in a pair the leader's barriers count the follower's
+            // bytes too, and neither CTA exits before the final cluster
+            // barrier). Issue i went to stage i % stages with parity
             // (i / stages) & 1; only the newest issue per stage can be pending.
             const long long first = issued > stages ? issued - stages : 0;
             for (long long i = first; i < issued; ++i) {
@@ -198,15 +243,16 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                           kErrTimeoutDrain);
             }
         }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1 && lane == 0 && leader) {
         // ------------------------------------------------------ MMA issuer
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, p.err, kErrTimeoutMma)) {
+        for (int tile = unit; tile < num_tiles && ok; tile += num_units) {
+            if (!mbar_wait<CG == 2>(tempty_bar(acc), acc_phase ^ 1u, abort_flag, p.err,
+                                    kErrTimeoutMma)) {
                 ok = false;
                 break;
             }
@@ -227,18 +273,26 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                     for (int h = 0; h < T::kMHalves; ++h) {
                         const uint64_t adesc = make_smem_desc<T::kSwizzle>(
                             sa + h * 128 * BK * 2 + kk * T::kUmmaK * 2);
-                        umma_f16<1>(d_base + h * BN, adesc, bdesc, T::kIdesc,
-                                    (kb > 0 || kk > 0) ? 1u : 0u);
+                        umma_f16<CG>(d_base + h * BN, adesc, bdesc, T::kIdesc,
+                                     (kb > 0 || kk > 0) ? 1u : 0u);
                     }
                 }
-                umma_commit(empty_bar(stage));  // frees the stage when these MMAs finish
+                // Free the stage (in both CTAs of a pair) when these MMAs finish.
+                if constexpr (CG == 1)
+                    umma_commit(empty_bar(stage));
+                else
+                    umma_commit_pair(empty_bar(stage), 0x3);
                 if (++stage == stages) {
                     stage = 0;
                     phase ^= 1u;
                 }
             }
             if (!ok) break;
-            umma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+            // Accumulator ready for the epilogue (of both CTAs of a pair).
+            if constexpr (CG == 1)
+                umma_commit(tfull_bar(acc));
+            else
+                umma_commit_pair(tfull_bar(acc), 0x3);
             if (++acc == T::kAccBufs) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -246,7 +300,10 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         }
         if (!ok) {
             // Abort path: wait for every MMA already issued before TMEM is freed.
-            umma_commit(drain_bar);
+            if constexpr (CG == 1)
+                umma_commit(drain_bar);
+            else
+                umma_commit_pair(drain_bar, 0x1);
             mbar_wait(drain_bar, 0, nullptr, p.err, kErrTimeoutDrain);
         }
     } else if (warp >= 2) {
@@ -257,9 +314,13 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         constexpr int kGroups = WARPS / 4;
         constexpr int kChunks = BN / 32;  // 32 FP32 columns per tcgen05.ld
         const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+        // Remote (leader) accumulator-empty barrier for the follower of a pair.
+        const uint32_t tempty0 = CG == 2 ? map_to_cta(tempty_bar(0), 0) : tempty_bar(0);
+        const uint32_t stage_buf0 = epi_base + uint32_t(epi * 2 * T::kEpiChunkBytes);
+        int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (int tile = unit; tile < num_tiles; tile += num_units) {
             int tm, tn;
             tile_coords(tile, num_m, num_n, p.groupM, tm, tn);
             int ok = 1;
@@ -270,30 +331,52 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             tc_fence_after();
 #pragma unroll
             for (int h = 0; h < T::kMHalves; ++h) {
-                // M=128 UMMA: row r lives in TMEM lane r. M=64 UMMA: rows
-                // 16q..16q+15 live in lanes 32q..32q+15 of sub-partition q.
-                const int row_in_tile =
-                    BM == 64 ? quad * 16 + lane : h * 128 + quad * 32 + lane;
+                // M=128 / 256-pair UMMA: row r of this CTA lives in TMEM lane r.
+                // M=64 UMMA: rows 16q..16q+15 live in lanes 32q..32q+15.
+                const int warp_row0 = BM == 64 ? quad * 16 : h * 128 + quad * 32;
+                const int tile_row0 = tm * BM + int(rank) * T::kRowsA;
                 const bool row_live = (BM != 64 || lane < 16);
-                const long long row = (long long)tm * BM + row_in_tile;
+                const long long row = (long long)tile_row0 + warp_row0 + lane;
                 const bool row_ok = row_live && row < p.M;
-                __half* crow = p.C + row * p.ldc;
-#pragma unroll
+#pragma unroll 1
                 for (int j = group; j < kChunks; j += kGroups) {
                     uint32_t r[32];
                     const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) +
                                            uint32_t(acc * T::kAccCols + h * BN + j * 32);
                     tmem_ld_32x32b_x32(taddr, r);
                     tmem_wait_ld();
-                    const int col0 = tn * BN + j * 32;
-                    if (row_ok) {
-                        uint32_t packed[16];
+                    uint32_t packed[16];
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            __half2 h2 = __floats2half2_rn(__uint_as_float(r[2 * e]),
-                                                           __uint_as_float(r[2 * e + 1]));
-                            packed[e] = *reinterpret_cast<uint32_t*>(&h2);
+                    for (int e = 0; e < 16; ++e)
+                        packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                    const int col0 = tn * BN + j * 32;
+                    if (p.tma_store) {
+                        // Stage this warp's 32 x 32 chunk (one 64-byte row per
+                        // lane, 64B-swizzled: 16-byte unit c of row r sits at
+                        // unit c ^ ((r >> 1) & 3), conflict-free) and hand it to
+                        // a TMA store, which clips rows/columns outside C.
+                        const uint32_t sbuf = stage_buf0 + uint32_t(buf * T::kEpiChunkBytes);
+                        if (lane == 0) tma_store_wait_read<1>();  // buffer's previous store has read it
+                        __syncwarp();
+                        const uint32_t row_addr = sbuf + uint32_t(lane * 64);
+                        const uint32_t sw = uint32_t((lane >> 1) & 3);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                             row_addr + ((uint32_t(c) ^ sw) << 4)),
+                                         "r"(packed[4 * c]), "r"(packed[4 * c + 1]),
+                                         "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
+                                         : "memory");
                         }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0);
+                            tma_store_commit();
+                        }
+                        buf ^= 1;
+                    } else if (row_ok) {
+                        __half* crow = p.C + row * p.ldc;
                         if (vec_ok && col0 + 32 <= p.N) {
                             uint4* dst = reinterpret_cast<uint4*>(crow + col0);
 #pragma unroll
@@ -301,28 +384,43 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                                 dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1],
                                                     packed[4 * v + 2], packed[4 * v + 3]);
                         } else {
-                            const __half* hv = reinterpret_cast<const __half*>(packed);
-                            for (int e = 0; e < 32 && col0 + e < p.N; ++e) crow[col0 + e] = hv[e];
+                            for (int e = 0; e < 32 && col0 + e < p.N; ++e) {
+                                const uint32_t w = packed[e >> 1];
+                                const unsigned short bits =
+                                    (e & 1) ? (unsigned short)(w >> 16) : (unsigned short)(w & 0xffff);
+                                crow[col0 + e] = __ushort_as_half(bits);
+                            }
                         }
                     }
                 }
             }
+            // Every TMEM read of this accumulator is done: hand it back.
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(acc));
+            if (lane == 0) {
+                if constexpr (CG == 1)
+                    mbar_arrive(tempty_bar(acc));
+                else
+                    mbar_arrive_cluster(tempty0 + 8u * acc);
+            }
             if (++acc == T::kAccBufs) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
+        if (p.tma_store && lane == 0) tma_store_wait_all<0>();
     }
 
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) {
+        cluster_sync();  // neither CTA frees TMEM or exits while its peer may still use it
+    } else {
+        __syncthreads();
+    }
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc<1>(tmem_base, T::kTmemCols);
+        tmem_dealloc<CG>(tmem_base, T::kTmemCols);
     }
 }
 

@@ -37,6 +37,10 @@ CONFIGS = [
     (256, 128, 64, 3, 4, 8),
     (256, 256, 32, 3, 8, 16),
     (64, 256, 64, 4, 4, 2),
+    (256, 128, 64, 4, 4, 8, 2),   # 2-CTA pair tiles
+    (256, 256, 64, 4, 8, 8, 2),
+    (256, 64, 32, 3, 4, 3, 2),
+    (256, 128, 32, 2, 8, 8, 1),   # single-CTA 256-row tile
 ]
 
 
@@ -61,7 +65,8 @@ RAGGED = [(200, 136, 72), (1, 8, 8), (129, 257, 33), (64, 64, 16), (300, 520, 10
 
 
 @pytest.mark.parametrize("shape", RAGGED, ids=lambda s: "%dx%dx%d" % s)
-@pytest.mark.parametrize("c", [CONFIGS[0], CONFIGS[1], CONFIGS[3], CONFIGS[5]],
+@pytest.mark.parametrize("c", [CONFIGS[0], CONFIGS[1], CONFIGS[3], CONFIGS[5], CONFIGS[8],
+                               CONFIGS[10]],
                          ids=lambda c: "x".join(map(str, c)))
 def test_ragged_shapes(shape, c):
     M, N, K = shape
@@ -88,3 +93,50 @@ def test_every_registered_variant():
     for v in rb.variants():
         out = run_gemm(v.config, ad, bd, M, N, K)
         assert_close(to_host_bits(out), ref, v.config.tag())
+
+
+@pytest.mark.parametrize("c", [CONFIGS[0], CONFIGS[3], CONFIGS[8]], ids=lambda c: "x".join(map(str, c)))
+def test_padded_ldc_leaves_padding_untouched(c):
+    """C with a padded row pitch: the epilogue's clipped TMA stores must not
+    write the padding columns (sentinel NaN survives)."""
+    M, N, K = 300, 200, 128
+    a, b = oracle.unit_inputs(M, N, K, seed=11)
+    ref = oracle.gemm_f64(a, b)
+    cfg = _cfg(*c)
+    out = run_gemm(cfg, to_dev(a), to_dev(b), M, N, K, ldc=N + 24)
+    bits = to_host_bits(out)
+    assert np.isnan(bits[:, N:].view(np.float16).astype(np.float32)).all()
+    assert_close(np.ascontiguousarray(bits[:, :N]), ref, cfg.tag())
+
+
+@pytest.mark.parametrize("c", [CONFIGS[0], CONFIGS[4], CONFIGS[8]], ids=lambda c: "x".join(map(str, c)))
+def test_unaligned_c_uses_direct_stores(c):
+    """A C pointer that is not 16-byte aligned, or a pitch that is not a
+    multiple of 8, takes the register-to-global epilogue; results must match."""
+    M, N, K = 130, 77, 64
+    a, b = oracle.unit_inputs(M, N, K, seed=5)
+    ref = oracle.gemm_f64(a, b)
+    cfg = _cfg(*c)
+    ldc = N + 2
+    buf = torch.full((M * ldc + 8,), float("nan"), dtype=torch.float16, device="cuda")
+    cview = buf[1:1 + M * ldc]           # 2-byte offset: not 16-byte aligned
+    ad, bd = to_dev(a), to_dev(b)
+    st = rb.launch_raw(cfg, ad.data_ptr(), bd.data_ptr(), cview.data_ptr(), M, N, K, K, K, ldc,
+                       torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert rb.device_error() == 0
+    got = to_host_bits(cview).reshape(M, ldc)
+    assert np.isnan(got[:, N:].view(np.float16).astype(np.float32)).all()
+    assert_close(np.ascontiguousarray(got[:, :N]), ref, cfg.tag())
+
+
+def test_k_zero_writes_zeros():
+    M, N = 64, 48
+    cfg = _cfg(*CONFIGS[0])
+    a = torch.empty((M, 8), dtype=torch.float16, device="cuda")
+    b = torch.empty((N, 8), dtype=torch.float16, device="cuda")
+    c = torch.full((M, N), 3.0, dtype=torch.float16, device="cuda")
+    assert rb.launch_raw(cfg, a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, 0, 8, 8, N, 0) == 0
+    torch.cuda.synchronize()
+    assert bool((c == 0).all())

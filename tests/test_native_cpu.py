@@ -32,23 +32,42 @@ def test_every_declared_function_has_a_python_signature():
     assert sorted(SIGNATURES) == declared_functions()
 
 
+def _smem_bytes(bm, bn, bk, s, w, cg):
+    """Shared memory one CTA needs: operand ring + epilogue staging + fixed."""
+    return 1024 + s * (bm // cg + bn // cg) * bk * 2 + w * 2 * 2048 + 256
+
+
 def test_variant_table_is_the_valid_grid():
-    """BM, BN in {64,128,256} x BK in {32,64} x stages 2..5 x warps {4,8} = 144
-    points; exactly the four whose operand ring overflows 227 KB of shared
-    memory are dropped."""
+    """BM, BN in {64,128,256} x BK in {32,64} x stages 2..5 x warps {4,8}, with
+    BM=256 both as a 2-CTA pair and as one CTA: every point whose shared memory
+    fits in 227 KB is registered, every other point is refused. The four grid
+    points whose operand ring alone overflows are among the refused."""
     vs = rb.variants()
-    keys = {(v.config.BM, v.config.BN, v.config.BK, v.config.stages, v.config.warps) for v in vs}
-    assert len(vs) == len(keys) == 144 - 4 * 2
+    keys = {(v.config.BM, v.config.BN, v.config.BK, v.config.stages, v.config.warps,
+             v.config.cta_group) for v in vs}
+    assert len(vs) == len(keys)
+    expected = set()
+    for bm in (64, 128, 256):
+        for bn in (64, 128, 256):
+            for bk in (32, 64):
+                for s in (2, 3, 4, 5):
+                    for w in (4, 8):
+                        for cg in ((1, 2) if bm == 256 else (1,)):
+                            fits = _smem_bytes(bm, bn, bk, s, w, cg) <= 232448
+                            assert rb.config_ok(TileConfig(bm, bn, bk, s, w, 8, cg)) == fits
+                            if fits:
+                                expected.add((bm, bn, bk, s, w, cg))
+    assert keys == expected
     for bm, bn, bk, s in [(128, 256, 64, 5), (256, 128, 64, 5), (256, 256, 64, 4),
                           (256, 256, 64, 5)]:
         for w in (4, 8):
-            assert (bm, bn, bk, s, w) not in keys
-            assert not rb.config_ok(TileConfig(bm, bn, bk, s, w, 8))
+            assert (bm, bn, bk, s, w, 1) not in keys
     for v in vs:
         assert v.smem_bytes <= 232448
         assert v.tmem_cols in (64, 128, 256, 512)
         assert v.threads == (2 + v.config.warps) * 32
         assert v.config.groupM == 8
+        assert v.cluster_size == v.config.cta_group
 
 
 @pytest.mark.parametrize("bad", [
