@@ -178,6 +178,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         tmem_relinquish<CG>();
     }
     tc_fence_before();
+    __syncwarp();  // barrier.cluster is .aligned: every warp arrives converged
     if constexpr (CG == 2) {
         cluster_sync();  // both CTAs' barriers and TMEM exist before any remote use
     } else {
@@ -412,6 +413,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     }
 
     tc_fence_before();
+    __syncwarp();
     if constexpr (CG == 2) {
         cluster_sync();  // neither CTA frees TMEM or exits while its peer may still use it
     } else {
