@@ -47,6 +47,10 @@ const char* ridge_status_string(int status);
  *   cta_group 1 = one CTA per tile; 2 = BM=256 tile computed by a 2-CTA cluster
  *            with cta_group::2 MMAs (each CTA holds 128 rows). 0 = default
  *            (2 for BM=256, else 1).
+ *   split_k  0 = automatic split-K tail: when the tiles leave the last round of
+ *            the persistent grid partly idle, that round's tiles are split along
+ *            K over the idle units and reduced through an FP32 workspace;
+ *            1 = never split (every tile is computed whole by one unit).
  */
 typedef struct ridge_tile_config {
     int32_t BM, BN, BK;
@@ -54,6 +58,7 @@ typedef struct ridge_tile_config {
     int32_t warps;
     int32_t groupM;
     int32_t cta_group;
+    int32_t split_k;
 } ridge_tile_config;
 
 /*
@@ -110,6 +115,25 @@ int ridge_config_valid_for_shape(const ridge_tile_config* cfg, int64_t M, int64_
 int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
                       int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                       void* stream);
+
+/*
+ * Device workspace (bytes) a launch of `cfg` on M x N x K needs on the current
+ * device for its split-K tail; 0 when the launch does not split. Deterministic
+ * for a given config, shape and device.
+ */
+int ridge_gemm_workspace_size(const ridge_tile_config* cfg, int64_t M, int64_t N, int64_t K,
+                              int64_t* bytes);
+
+/*
+ * ridge_gemm_launch with a caller-owned workspace of at least
+ * ridge_gemm_workspace_size bytes (256-byte aligned). Its counter area must be
+ * zero before the first launch (e.g. cudaMemset once); every launch leaves it
+ * zero again. Launches that share one workspace must be ordered (one stream).
+ * ridge_gemm_launch itself keeps such a workspace per device and stream.
+ */
+int ridge_gemm_launch_ws(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                         int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                         void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Same, addressing the variant by its table index. */
 int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,

@@ -26,7 +26,8 @@ BOTTLENECKS = ["TENSOR_CORE", "SMEM", "HBM", "OCC", "WAVES", "ENVELOPE", "DOES_N
 
 class TileConfigC(C.Structure):
     _fields_ = [("BM", C.c_int32), ("BN", C.c_int32), ("BK", C.c_int32), ("stages", C.c_int32),
-                ("warps", C.c_int32), ("groupM", C.c_int32), ("cta_group", C.c_int32)]
+                ("warps", C.c_int32), ("groupM", C.c_int32), ("cta_group", C.c_int32),
+                ("split_k", C.c_int32)]
 
 
 class VariantInfoC(C.Structure):
@@ -92,6 +93,10 @@ SIGNATURES = {
                                               _i64, _i64]),
     "ridge_gemm_launch": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _vp]),
+    "ridge_gemm_workspace_size": (C.c_int, [C.POINTER(TileConfigC), _i64, _i64, _i64,
+                                            C.POINTER(_i64)]),
+    "ridge_gemm_launch_ws": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
+                                       _i64, _i64, _i64, _vp, _i64, _vp]),
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                             _i64, _i64, _vp]),
     "ridge_device_error": (C.c_int, [C.c_int, C.POINTER(_i32)]),

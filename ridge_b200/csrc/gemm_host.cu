@@ -15,6 +15,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -185,7 +186,7 @@ const std::vector<ridge_tile_config>& variant_table() {
                     for (int s : stages)
                         for (int w : warps)
                             for (int cg = 1; cg <= (bm == 256 ? 2 : 1); ++cg) {
-                                ridge_tile_config c{bm, bn, bk, s, w, 8, cg};
+                                ridge_tile_config c{bm, bn, bk, s, w, 8, cg, 0};
                                 if (ridge_config_check(&c, nullptr) == RIDGE_OK) t.push_back(c);
                             }
         return t;
@@ -210,6 +211,205 @@ void fill_info(const KernelEntry& e, const ridge_tile_config& c, ridge_variant_i
         info->regs_per_thread = fa.numRegs;
     else
         cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ launch planning
+
+struct LaunchPlan {
+    const KernelEntry* e = nullptr;
+    int idx = -1;
+    int smem = 0;
+    int grid_units = 0;  // CTAs (1-CTA kernels) or CTA pairs
+    int dp_tiles = 0, sk_tiles = 0, sk_splits = 1;
+    size_t ws_partials = 0;  // bytes of FP32 partial tiles
+    size_t ws_bytes = 0;     // total workspace (partials + counters)
+};
+
+// Co-resident tile units of `e` at depth `stages` on `dev`. 2-CTA pairs must
+// sit on one TPC, so those are asked of the runtime (once per kernel, depth
+// and device) rather than assumed to be SMs / 2.
+int64_t resident_units(const KernelEntry& e, int idx, int stages, int smem, DeviceState* dev) {
+    int64_t slots = int64_t(dev->num_sms / e.cta_group) * ctas_per_sm(e, stages);
+    if (e.cta_group > 1) {
+        std::atomic<int>& cached = dev->cluster_units[idx][stages];
+        int units = cached.load(std::memory_order_relaxed);
+        if (units == 0) {
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(unsigned(e.cta_group * 2), 1, 1);
+            lc.blockDim = dim3(unsigned(e.threads), 1, 1);
+            lc.dynamicSmemBytes = size_t(smem);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = unsigned(e.cta_group);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            lc.attrs = attr;
+            lc.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, e.func, &lc) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = int(slots);
+            }
+            units = n;
+            cached.store(units, std::memory_order_relaxed);
+        }
+        slots = std::min<int64_t>(slots, units);
+    }
+    return std::max<int64_t>(slots, 1);
+}
+
+int ensure_smem_attr(const KernelEntry& e, int idx, DeviceState* dev) {
+    if (!dev->smem_attr_set[idx].load(std::memory_order_acquire)) {
+        cudaError_t ce =
+            cudaFuncSetAttribute(e.func, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+        if (ce != cudaSuccess) return int(ce);
+        dev->smem_attr_set[idx].store(true, std::memory_order_release);
+    }
+    return RIDGE_OK;
+}
+
+// Grid size and split-K tail for one launch. With U resident units and T
+// tiles, whole tiles fill floor(T / U) rounds; the R = T mod U tiles of a
+// partial last round (all T when T < U) are split along K into
+// s = floor(U / R) ranges (at most 8, at most the K-block count) so the round
+// keeps R * s units busy instead of R. s < 2 means no split.
+int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, DeviceState* dev,
+              LaunchPlan* plan) {
+    int idx = -1;
+    const KernelEntry* e = find_entry(cfg, &idx);
+    if (!e) return RIDGE_EINVAL;
+    plan->e = e;
+    plan->idx = idx;
+    plan->smem = smem_for(*e, cfg.stages);
+    int st = ensure_smem_attr(*e, idx, dev);
+    if (st != RIDGE_OK) return st;
+    const int64_t tiles = ((M + e->BM - 1) / e->BM) * ((N + e->BN - 1) / e->BN);
+    const int64_t units = resident_units(*e, idx, cfg.stages, plan->smem, dev);
+    const int64_t num_kb = (K + e->BK - 1) / e->BK;
+    if (tiles > int64_t(1) << 30) return RIDGE_EINVAL;
+    plan->grid_units = int(std::min(tiles, units));
+    plan->dp_tiles = int(tiles);
+    plan->sk_tiles = 0;
+    plan->sk_splits = 1;
+    plan->ws_partials = plan->ws_bytes = 0;
+    if (cfg.split_k == 1) return RIDGE_OK;
+    const int64_t rem = tiles >= units ? tiles % units : tiles;
+    if (rem == 0) return RIDGE_OK;
+    const int64_t s = std::min<int64_t>(std::min<int64_t>(units / rem, 8), num_kb);
+    if (s < 2) return RIDGE_OK;
+    plan->dp_tiles = int(tiles - rem);
+    plan->sk_tiles = int(rem);
+    plan->sk_splits = int(s);
+    plan->grid_units = int(std::max<int64_t>(std::min(tiles, units), rem * s));
+    const size_t tile_floats = size_t(e->tile_a_rows) * e->BN;
+    plan->ws_partials = (size_t(rem) * (s - 1) * e->cta_group * tile_floats * 4 + 255) / 256 * 256;
+    plan->ws_bytes = plan->ws_partials + size_t(rem) * e->cta_group * e->warps * 4;
+    return RIDGE_OK;
+}
+
+// Library-owned split-K workspaces, one per (device, stream), grown on demand
+// and zeroed when (re)allocated; kernels leave their counters at zero.
+struct WorkspaceCache {
+    std::mutex mu;
+    std::map<cudaStream_t, std::pair<void*, size_t>> by_stream;
+};
+WorkspaceCache g_ws[kMaxDevices];
+
+int cached_workspace(int device, cudaStream_t stream, size_t bytes, void** out) {
+    WorkspaceCache& c = g_ws[device];
+    std::lock_guard<std::mutex> lock(c.mu);
+    auto& slot = c.by_stream[stream];
+    if (slot.second < bytes) {
+        if (slot.first) {
+            cudaError_t ce = cudaStreamSynchronize(stream);
+            if (ce != cudaSuccess) return int(ce);
+            cudaFree(slot.first);
+            slot = {nullptr, 0};
+        }
+        void* p = nullptr;
+        const size_t want = std::max<size_t>(bytes, size_t(1) << 20);
+        cudaError_t ce = cudaMalloc(&p, want);
+        if (ce != cudaSuccess) return int(ce);
+        ce = cudaMemsetAsync(p, 0, want, stream);
+        if (ce != cudaSuccess) {
+            cudaFree(p);
+            return int(ce);
+        }
+        slot = {p, want};
+    }
+    *out = slot.first;
+    return RIDGE_OK;
+}
+
+int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, void* C, int64_t M,
+                  int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream_v,
+                  bool caller_ws, void* workspace, int64_t workspace_bytes) {
+    int st = ridge_config_valid_for_shape(cfg, M, N, K, lda, ldb, ldc);
+    if (st != RIDGE_OK) return st;
+    if (M == 0 || N == 0) return RIDGE_OK;
+    if (!A || !B || !C) return RIDGE_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+        (reinterpret_cast<uintptr_t>(C) & 1))
+        return RIDGE_EINVAL;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    DeviceState* dev = device_state(&st);
+    if (!dev) return st;
+    if (K == 0) {
+        cudaError_t e = cudaMemset2DAsync(C, size_t(ldc) * 2, 0, size_t(N) * 2, size_t(M), stream);
+        return int(e);
+    }
+    LaunchPlan plan;
+    st = make_plan(*cfg, M, N, K, dev, &plan);
+    if (st != RIDGE_OK) return st;
+    const KernelEntry* e = plan.e;
+
+    void* ws = nullptr;
+    if (plan.ws_bytes > 0) {
+        if (caller_ws) {
+            if (!workspace || workspace_bytes < int64_t(plan.ws_bytes) ||
+                (reinterpret_cast<uintptr_t>(workspace) & 255))
+                return RIDGE_EINVAL;
+            ws = workspace;
+        } else {
+            int device = 0;
+            cudaGetDevice(&device);
+            st = cached_workspace(device, stream, plan.ws_bytes, &ws);
+            if (st != RIDGE_OK) return st;
+        }
+    }
+
+    CUtensorMap tmap_a, tmap_b, tmap_c;
+    st = make_operand_map(&tmap_a, A, M, K, lda, e->tile_a_rows, e->BK);
+    if (st != RIDGE_OK) return st;
+    st = make_operand_map(&tmap_b, B, N, K, ldb, e->tile_b_rows, e->BK);
+    if (st != RIDGE_OK) return st;
+    // The TMA-store epilogue needs a 16-byte aligned C with a 16-byte row
+    // pitch; otherwise the kernel stores directly from registers.
+    const bool tma_store = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && (ldc % 8) == 0;
+    std::memset(&tmap_c, 0, sizeof(tmap_c));
+    if (tma_store) {
+        st = make_output_map(&tmap_c, C, M, N, ldc, e->epi_rows);
+        if (st != RIDGE_OK) return st;
+    }
+
+    GemmParams p;
+    p.C = static_cast<__half*>(C);
+    p.M = int(M);
+    p.N = int(N);
+    p.K = int(K);
+    p.ldc = ldc;
+    p.groupM = cfg->groupM;
+    p.stages = cfg->stages;
+    p.tma_store = tma_store ? 1 : 0;
+    p.err = dev->err_word;
+    p.dp_tiles = plan.dp_tiles;
+    p.sk_tiles = plan.sk_tiles;
+    p.sk_splits = plan.sk_splits;
+    p.workspace = static_cast<float*>(ws);
+    p.counters = ws ? reinterpret_cast<int*>(static_cast<char*>(ws) + plan.ws_partials) : nullptr;
+    cudaError_t ce = e->launch(&tmap_a, &tmap_b, &tmap_c, &p, plan.grid_units * e->cta_group,
+                               plan.smem, stream);
+    return int(ce);
 }
 
 }  // namespace
@@ -237,6 +437,7 @@ int ridge_config_check(const ridge_tile_config* cfg, ridge_variant_info* info) {
     if (!cfg) return RIDGE_EINVAL;
     const ridge_tile_config& c = *cfg;
     if (c.stages < 2 || c.stages > kMaxStages || c.groupM < 1) return RIDGE_EINVAL;
+    if (c.split_k != 0 && c.split_k != 1) return RIDGE_EINVAL;
     const KernelEntry* e = find_entry(c);
     if (!e) return RIDGE_EINVAL;
     if (smem_for(*e, c.stages) > kMaxDynSmem) return RIDGE_EINVAL;
@@ -278,93 +479,34 @@ int ridge_config_valid_for_shape(const ridge_tile_config* cfg, int64_t M, int64_
     return RIDGE_OK;
 }
 
-int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
-                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
-                      void* stream_v) {
-    int st = ridge_config_valid_for_shape(cfg, M, N, K, lda, ldb, ldc);
+int ridge_gemm_workspace_size(const ridge_tile_config* cfg, int64_t M, int64_t N, int64_t K,
+                              int64_t* bytes) {
+    if (!bytes) return RIDGE_EINVAL;
+    int st = ridge_config_valid_for_shape(cfg, M, N, K, std::max<int64_t>(K, 8),
+                                          std::max<int64_t>(K, 8), N);
     if (st != RIDGE_OK) return st;
-    if (M == 0 || N == 0) return RIDGE_OK;
-    if (!A || !B || !C) return RIDGE_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
-        (reinterpret_cast<uintptr_t>(C) & 1))
-        return RIDGE_EINVAL;
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    *bytes = 0;
+    if (M == 0 || N == 0 || K == 0) return RIDGE_OK;
     DeviceState* dev = device_state(&st);
     if (!dev) return st;
-    if (K == 0) {
-        cudaError_t e = cudaMemset2DAsync(C, size_t(ldc) * 2, 0, size_t(N) * 2, size_t(M), stream);
-        return int(e);
-    }
-
-    int idx = -1;
-    const KernelEntry* e = find_entry(*cfg, &idx);
-    const int smem = smem_for(*e, cfg->stages);
-    if (!dev->smem_attr_set[idx].load(std::memory_order_acquire)) {
-        cudaError_t ce =
-            cudaFuncSetAttribute(e->func, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-        if (ce != cudaSuccess) return int(ce);
-        dev->smem_attr_set[idx].store(true, std::memory_order_release);
-    }
-
-    CUtensorMap tmap_a, tmap_b, tmap_c;
-    st = make_operand_map(&tmap_a, A, M, K, lda, e->tile_a_rows, e->BK);
+    LaunchPlan plan;
+    st = make_plan(*cfg, M, N, K, dev, &plan);
     if (st != RIDGE_OK) return st;
-    st = make_operand_map(&tmap_b, B, N, K, ldb, e->tile_b_rows, e->BK);
-    if (st != RIDGE_OK) return st;
-    // The TMA-store epilogue needs a 16-byte aligned C with a 16-byte row
-    // pitch; otherwise the kernel stores directly from registers.
-    const bool tma_store =
-        (reinterpret_cast<uintptr_t>(C) & 15) == 0 && (ldc % 8) == 0;
-    std::memset(&tmap_c, 0, sizeof(tmap_c));
-    if (tma_store) {
-        st = make_output_map(&tmap_c, C, M, N, ldc, e->epi_rows);
-        if (st != RIDGE_OK) return st;
-    }
+    *bytes = int64_t(plan.ws_bytes);
+    return RIDGE_OK;
+}
 
-    GemmParams p;
-    p.C = static_cast<__half*>(C);
-    p.M = int(M);
-    p.N = int(N);
-    p.K = int(K);
-    p.ldc = ldc;
-    p.groupM = cfg->groupM;
-    p.stages = cfg->stages;
-    p.tma_store = tma_store ? 1 : 0;
-    p.err = dev->err_word;
+int ridge_gemm_launch_ws(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                         int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                         void* workspace, int64_t workspace_bytes, void* stream) {
+    return launch_common(cfg, A, B, C, M, N, K, lda, ldb, ldc, stream, true, workspace,
+                         workspace_bytes);
+}
 
-    const int64_t tiles = ((M + e->BM - 1) / e->BM) * ((N + e->BN - 1) / e->BN);
-    int64_t slots = int64_t(dev->num_sms / e->cta_group) * ctas_per_sm(*e, cfg->stages);
-    if (e->cta_group > 1) {
-        // Co-resident clusters: pairs must sit on one TPC, so ask the runtime
-        // (once per kernel, depth and device) rather than assume SMs / 2.
-        std::atomic<int>& cached = dev->cluster_units[idx][cfg->stages];
-        int units = cached.load(std::memory_order_relaxed);
-        if (units == 0) {
-            cudaLaunchConfig_t lc = {};
-            lc.gridDim = dim3(unsigned(e->cta_group * 2), 1, 1);
-            lc.blockDim = dim3(unsigned(e->threads), 1, 1);
-            lc.dynamicSmemBytes = size_t(smem);
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = unsigned(e->cta_group);
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            lc.attrs = attr;
-            lc.numAttrs = 1;
-            int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, e->func, &lc) != cudaSuccess || n <= 0) {
-                cudaGetLastError();
-                n = int(slots);
-            }
-            units = n;
-            cached.store(units, std::memory_order_relaxed);
-        }
-        slots = std::min<int64_t>(slots, units);
-    }
-    const int grid_units = int(std::min<int64_t>(tiles, std::max<int64_t>(slots, 1)));
-    cudaError_t ce =
-        e->launch(&tmap_a, &tmap_b, &tmap_c, &p, grid_units * e->cta_group, smem, stream);
-    return int(ce);
+int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                      void* stream) {
+    return launch_common(cfg, A, B, C, M, N, K, lda, ldb, ldc, stream, false, nullptr, 0);
 }
 
 int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,

@@ -103,7 +103,53 @@ struct GemmParams {
     int stages;
     int tma_store;  // 1: epilogue stores through the C tensor map; 0: direct st.global
     int* err;
+    // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
+    // one per unit per round; the remaining sk_tiles tiles are each split into
+    // sk_splits contiguous K ranges, one range per unit, in a single last
+    // round. Split 0 of a tile owns it: it adds the FP32 partials the other
+    // splits leave in `workspace` and stores C. counters[(sk * CG + rank) *
+    // warps + warp] counts partial chunks published for one owner warp; the
+    // owner resets it to 0 after consuming, so it starts at 0 every launch.
+    int dp_tiles;
+    int sk_tiles;
+    int sk_splits;
+    float* workspace;
+    int* counters;
 };
+
+// One unit of work: a tile and the K-block range [kb0, kb1) to accumulate.
+// split < 0 marks a whole (data-parallel) tile.
+struct WorkItem {
+    int tile, kb0, kb1, split, sk;
+};
+
+__device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_units, int num_kb,
+                                         int i, WorkItem& w) {
+    const int dp_count = p.dp_tiles > unit ? (p.dp_tiles - unit + num_units - 1) / num_units : 0;
+    if (i < dp_count) {
+        w.tile = unit + i * num_units;
+        w.kb0 = 0;
+        w.kb1 = num_kb;
+        w.split = -1;
+        w.sk = -1;
+        return true;
+    }
+    if (i == dp_count && unit < p.sk_tiles * p.sk_splits) {
+        w.sk = unit / p.sk_splits;
+        w.split = unit - w.sk * p.sk_splits;
+        w.tile = p.dp_tiles + w.sk;
+        w.kb0 = int((long long)num_kb * w.split / p.sk_splits);
+        w.kb1 = int((long long)num_kb * (w.split + 1) / p.sk_splits);
+        return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
 
 // Grouped-M tile order, the same mapping as the reference launch order
 // (gemm-mma.cuh:158-178): tiles are taken groupM row-tiles at a time, column by
@@ -189,7 +235,6 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
 
     const int num_m = (p.M + BM - 1) / BM;
     const int num_n = (p.N + BN - 1) / BN;
-    const int num_tiles = num_m * num_n;
     const int num_kb = (p.K + BK - 1) / BK;
     const int unit = blockIdx.x / CG;
     const int num_units = gridDim.x / CG;
@@ -203,12 +248,13 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         uint32_t phase = 0;
         long long issued = 0;
         bool ok = true;
-        for (int tile = unit; tile < num_tiles && ok; tile += num_units) {
+        WorkItem w;
+        for (int it = 0; ok && get_item(p, unit, num_units, num_kb, it, w); ++it) {
             int tm, tn;
-            tile_coords(tile, num_m, num_n, p.groupM, tm, tn);
+            tile_coords(w.tile, num_m, num_n, p.groupM, tm, tn);
             const int a_row = tm * BM + int(rank) * T::kRowsA;
             const int b_row = tn * BN + int(rank) * T::kRowsB;
-            for (int kb = 0; kb < num_kb; ++kb) {
+            for (int kb = w.kb0; kb < w.kb1; ++kb) {
                 if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err,
                                kErrTimeoutProducer)) {
                     ok = false;
@@ -251,7 +297,8 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        for (int tile = unit; tile < num_tiles && ok; tile += num_units) {
+        WorkItem w;
+        for (int it = 0; ok && get_item(p, unit, num_units, num_kb, it, w); ++it) {
             if (!mbar_wait<CG == 2>(tempty_bar(acc), acc_phase ^ 1u, abort_flag, p.err,
                                     kErrTimeoutMma)) {
                 ok = false;
@@ -259,7 +306,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             }
             tc_fence_after();
             const uint32_t d_base = tmem_base + uint32_t(acc * T::kAccCols);
-            for (int kb = 0; kb < num_kb; ++kb) {
+            for (int kb = w.kb0; kb < w.kb1; ++kb) {
                 if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err, kErrTimeoutMma)) {
                     ok = false;
                     break;
@@ -275,7 +322,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                         const uint64_t adesc = make_smem_desc<T::kSwizzle>(
                             sa + h * 128 * BK * 2 + kk * T::kUmmaK * 2);
                         umma_f16<CG>(d_base + h * BN, adesc, bdesc, T::kIdesc,
-                                     (kb > 0 || kk > 0) ? 1u : 0u);
+                                     (kb > w.kb0 || kk > 0) ? 1u : 0u);
                     }
                 }
                 // Free the stage (in both CTAs of a pair) when these MMAs finish.
@@ -321,15 +368,41 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = unit; tile < num_tiles; tile += num_units) {
+        WorkItem w;
+        for (int it = 0; get_item(p, unit, num_units, num_kb, it, w); ++it) {
             int tm, tn;
-            tile_coords(tile, num_m, num_n, p.groupM, tm, tn);
+            tile_coords(w.tile, num_m, num_n, p.groupM, tm, tn);
             int ok = 1;
             if (lane == 0)
                 ok = mbar_wait(tfull_bar(acc), acc_phase, abort_flag, p.err, kErrTimeoutEpilogue);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
+            // Split-K bookkeeping for this item: where this CTA's FP32 partial
+            // tiles live, and (owner) the counter its partial chunks bump.
+            constexpr long long kTileFloats = (long long)T::kRowsA * BN;
+            float* ws_tile = nullptr;
+            int* counter = nullptr;
+            if (w.split >= 0) {
+                counter = p.counters + (w.sk * CG + int(rank)) * WARPS + epi;
+                const long long slot0 = (long long)w.sk * (p.sk_splits - 1);
+                ws_tile = p.workspace + (slot0 * CG + rank) * kTileFloats;
+            }
+            if (w.split == 0 && lane == 0) {
+                // Owner: wait until every other split published this warp's chunks.
+                const int want = p.sk_splits - 1;
+                if (ld_acquire_gpu(counter) < want) {
+                    const uint64_t t0 = global_timer_ns();
+                    while (ld_acquire_gpu(counter) < want) {
+                        if (global_timer_ns() - t0 > RIDGE_WAIT_LIMIT_NS) {
+                            *abort_flag = 1;
+                            atomicCAS(p.err, 0, int(kErrTimeoutSplitK));
+                            break;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
 #pragma unroll
             for (int h = 0; h < T::kMHalves; ++h) {
                 // M=128 / 256-pair UMMA: row r of this CTA lives in TMEM lane r.
@@ -346,6 +419,35 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                                            uint32_t(acc * T::kAccCols + h * BN + j * 32);
                     tmem_ld_32x32b_x32(taddr, r);
                     tmem_wait_ld();
+                    const long long ws_off = (long long)(warp_row0 + lane) * BN + j * 32;
+                    if (w.split > 0) {
+                        // Non-owner split: publish the FP32 partial chunk and move on.
+                        if (!row_live) continue;  // M=64: lanes 16-31 hold no rows
+                        float4* dst = reinterpret_cast<float4*>(
+                            ws_tile + (long long)(w.split - 1) * CG * kTileFloats + ws_off);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            __stcg(dst + v, make_float4(__uint_as_float(r[4 * v]),
+                                                        __uint_as_float(r[4 * v + 1]),
+                                                        __uint_as_float(r[4 * v + 2]),
+                                                        __uint_as_float(r[4 * v + 3])));
+                        continue;
+                    }
+                    if (w.split == 0 && row_live) {
+                        // Owner: add the other splits' partials, in split order.
+                        for (int sp = 1; sp < p.sk_splits; ++sp) {
+                            const float4* src = reinterpret_cast<const float4*>(
+                                ws_tile + (long long)(sp - 1) * CG * kTileFloats + ws_off);
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) {
+                                const float4 q = __ldcg(src + v);
+                                r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q.x);
+                                r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q.y);
+                                r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q.z);
+                                r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q.w);
+                            }
+                        }
+                    }
                     uint32_t packed[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
@@ -386,14 +488,22 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                                                     packed[4 * v + 2], packed[4 * v + 3]);
                         } else {
                             for (int e = 0; e < 32 && col0 + e < p.N; ++e) {
-                                const uint32_t w = packed[e >> 1];
-                                const unsigned short bits =
-                                    (e & 1) ? (unsigned short)(w >> 16) : (unsigned short)(w & 0xffff);
+                                const uint32_t word = packed[e >> 1];
+                                const unsigned short bits = (e & 1) ? (unsigned short)(word >> 16)
+                                                                    : (unsigned short)(word & 0xffff);
                                 crow[col0 + e] = __ushort_as_half(bits);
                             }
                         }
                     }
                 }
+            }
+            if (w.split > 0) {
+                // Make this warp's partial chunks visible, then count them.
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(counter, 1);
+            } else if (w.split == 0 && lane == 0) {
+                *counter = 0;  // consumed: ready for the next launch
             }
             // Every TMEM read of this accumulator is done: hand it back.
             tc_fence_before();

@@ -22,6 +22,7 @@ enum DeviceErr : int {
     kErrTimeoutMma = 2,        // MMA issuer waited too long for a full stage / free accumulator
     kErrTimeoutEpilogue = 3,   // epilogue waited too long for a finished accumulator
     kErrTimeoutDrain = 4,      // abort path: in-flight copies did not land in time
+    kErrTimeoutSplitK = 5,     // split-K owner waited too long for another split's partial
 };
 
 // Wall-clock budget for any single mbarrier wait, in nanoseconds. A healthy

@@ -26,18 +26,20 @@ class TileConfig:
     warps: int = 4
     groupM: int = 8
     cta_group: int = 0  # 0 = library default for this BM
+    split_k: int = 0    # 0 = automatic split-K tail, 1 = never split
 
     def to_c(self) -> TileConfigC:
         return TileConfigC(self.BM, self.BN, self.BK, self.stages, self.warps, self.groupM,
-                           self.cta_group)
+                           self.cta_group, self.split_k)
 
     @staticmethod
     def from_c(c: TileConfigC) -> "TileConfig":
-        return TileConfig(c.BM, c.BN, c.BK, c.stages, c.warps, c.groupM, c.cta_group)
+        return TileConfig(c.BM, c.BN, c.BK, c.stages, c.warps, c.groupM, c.cta_group, c.split_k)
 
     def tag(self) -> str:
-        return "%dx%dx%d_s%d_w%d_g%d_c%d" % (self.BM, self.BN, self.BK, self.stages, self.warps,
-                                             self.groupM, self.cta_group)
+        return "%dx%dx%d_s%d_w%d_g%d_c%d%s" % (self.BM, self.BN, self.BK, self.stages, self.warps,
+                                               self.groupM, self.cta_group,
+                                               "_nosplit" if self.split_k == 1 else "")
 
     def as_dict(self):
         return asdict(self)

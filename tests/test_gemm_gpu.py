@@ -140,3 +140,63 @@ def test_k_zero_writes_zeros():
     assert rb.launch_raw(cfg, a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, 0, 8, 8, N, 0) == 0
     torch.cuda.synchronize()
     assert bool((c == 0).all())
+
+
+# Split-K tail: (shape, config) pairs whose tile count leaves the last round of
+# the persistent grid partly idle, so the launcher splits tiles along K.
+SPLITK_CASES = [
+    ((512, 512, 4096), (128, 128, 64, 4, 4, 8)),          # 16 tiles -> 8-way split
+    ((16, 2048, 4096), (128, 256, 64, 4, 8, 8)),          # skinny M
+    ((512, 768, 2048), (256, 256, 64, 4, 4, 8, 2)),       # 2-CTA pairs, 8-way
+    ((1000, 1000, 1000), (128, 128, 32, 3, 4, 8)),        # ragged + 2-way
+    ((1280, 2048, 256), (128, 128, 64, 4, 4, 8)),         # whole rounds + split tail
+    ((2048, 2560, 512), (256, 256, 64, 4, 8, 8, 2)),      # pairs: whole rounds + split tail
+    ((640, 384, 1024), (64, 128, 64, 4, 4, 1)),           # M=64 UMMA rows
+]
+
+
+@pytest.mark.parametrize("shape,c", SPLITK_CASES, ids=lambda x: "x".join(map(str, x)))
+def test_split_k_tail(shape, c):
+    import ctypes
+    M, N, K = shape
+    cfg = _cfg(*c)
+    ws = ctypes.c_int64(0)
+    cc = cfg.to_c()
+    assert rb.lib.ridge_gemm_workspace_size(ctypes.byref(cc), M, N, K, ctypes.byref(ws)) == 0
+    assert ws.value > 0, "expected this case to split"
+    a, b = oracle.unit_inputs(M, N, K, seed=13)
+    ref = oracle.gemm_f64(a, b)
+    ad, bd = to_dev(a), to_dev(b)
+    for _ in range(2):  # twice: counters must come back to zero
+        out = run_gemm(cfg, ad, bd, M, N, K)
+        assert_close(to_host_bits(out), ref, "split " + cfg.tag())
+    import dataclasses
+    whole = run_gemm(dataclasses.replace(cfg, split_k=1), ad, bd, M, N, K)
+    assert_close(to_host_bits(whole), ref, "no split " + cfg.tag())
+
+
+def test_caller_workspace_launch():
+    """ridge_gemm_launch_ws on a caller-owned, zeroed workspace; a too-small
+    workspace is refused."""
+    import ctypes
+    M, N, K = 512, 512, 4096
+    cfg = _cfg(128, 128, 64, 4, 4, 8)
+    cc = cfg.to_c()
+    need = ctypes.c_int64(0)
+    assert rb.lib.ridge_gemm_workspace_size(ctypes.byref(cc), M, N, K, ctypes.byref(need)) == 0
+    ws = torch.zeros(need.value // 4 + 64, dtype=torch.int32, device="cuda")
+    a, b = oracle.unit_inputs(M, N, K, seed=17)
+    ref = oracle.gemm_f64(a, b)
+    ad, bd = to_dev(a), to_dev(b)
+    c = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert rb.lib.ridge_gemm_launch_ws(ctypes.byref(cc), ad.data_ptr(), bd.data_ptr(),
+                                       c.data_ptr(), M, N, K, K, K, N, ws.data_ptr(),
+                                       need.value - 4, s) == -1
+    for _ in range(2):
+        assert rb.lib.ridge_gemm_launch_ws(ctypes.byref(cc), ad.data_ptr(), bd.data_ptr(),
+                                           c.data_ptr(), M, N, K, K, K, N, ws.data_ptr(),
+                                           need.value, s) == 0
+        torch.cuda.synchronize()
+        assert rb.device_error() == 0
+        assert_close(to_host_bits(c), ref, "caller workspace")
