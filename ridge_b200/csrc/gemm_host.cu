@@ -301,7 +301,7 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     plan->sk_tiles = int(rem);
     plan->sk_splits = int(s);
     plan->grid_units = int(std::max<int64_t>(std::min(tiles, units), rem * s));
-    const size_t tile_floats = size_t(e->tile_a_rows) * e->BN;
+    const size_t tile_floats = size_t(e->partial_floats);
     plan->ws_partials = (size_t(rem) * (s - 1) * e->cta_group * tile_floats * 4 + 255) / 256 * 256;
     plan->ws_bytes = plan->ws_partials + size_t(rem) * e->cta_group * e->warps * 4;
     return RIDGE_OK;

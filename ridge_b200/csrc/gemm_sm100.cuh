@@ -86,6 +86,9 @@ struct GemmTraits {
     static constexpr int kEpiRowsPerWarp = BM == 64 ? 16 : 32;
     static constexpr int kEpiChunkBytes = 32 * 64;
     static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiChunkBytes;
+    // FP32 floats of one CTA's split-K partial tile: 128 lanes x BN per M-half
+    // (an M=64 tile keeps the 32-lane chunk layout, half of it unused).
+    static constexpr int kPartialFloats = kMHalves * 128 * BN;
     static constexpr int kBarrierBytes = 256;
     static constexpr int kAlignSlack = 1024;
     static constexpr uint32_t kIdesc = make_idesc_f16_f32(kUmmaM, BN);
@@ -380,7 +383,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             tc_fence_after();
             // Split-K bookkeeping for this item: where this CTA's FP32 partial
             // tiles live, and (owner) the counter its partial chunks bump.
-            constexpr long long kTileFloats = (long long)T::kRowsA * BN;
+            constexpr long long kTileFloats = T::kPartialFloats;
             float* ws_tile = nullptr;
             int* counter = nullptr;
             if (w.split >= 0) {
@@ -412,39 +415,50 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 const bool row_live = (BM != 64 || lane < 16);
                 const long long row = (long long)tile_row0 + warp_row0 + lane;
                 const bool row_ok = row_live && row < p.M;
+                // A warp whose rows all lie at or beyond M has nothing to reduce.
+                const bool warp_live = (long long)tile_row0 + warp_row0 < p.M;
 #pragma unroll 1
                 for (int j = group; j < kChunks; j += kGroups) {
                     uint32_t r[32];
                     const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) +
                                            uint32_t(acc * T::kAccCols + h * BN + j * 32);
+                    __syncwarp();
                     tmem_ld_32x32b_x32(taddr, r);
                     tmem_wait_ld();
-                    const long long ws_off = (long long)(warp_row0 + lane) * BN + j * 32;
+                    // Split-K partial chunks use a lane-contiguous layout: float4
+                    // v of lane L of chunk c sits at ((c * 8 + v) * 32 + L), so
+                    // every warp-wide store or load covers 512 contiguous bytes.
+                    // Producer and owner map warps to chunks identically.
+                    const long long chunk_id = (long long)(h * kChunks + j) * 4 + quad;
+                    const long long ws_off = chunk_id * 8 * 32 * 4 + lane * 4;
                     if (w.split > 0) {
-                        // Non-owner split: publish the FP32 partial chunk and move on.
-                        if (!row_live) continue;  // M=64: lanes 16-31 hold no rows
-                        float4* dst = reinterpret_cast<float4*>(
-                            ws_tile + (long long)(w.split - 1) * CG * kTileFloats + ws_off);
+                        // Non-owner split: publish the FP32 partial chunk.
+                        if (warp_live) {
+                            float4* dst = reinterpret_cast<float4*>(
+                                ws_tile + (long long)(w.split - 1) * CG * kTileFloats + ws_off);
 #pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            __stcg(dst + v, make_float4(__uint_as_float(r[4 * v]),
-                                                        __uint_as_float(r[4 * v + 1]),
-                                                        __uint_as_float(r[4 * v + 2]),
-                                                        __uint_as_float(r[4 * v + 3])));
-                        continue;
+                            for (int v = 0; v < 8; ++v)
+                                __stcg(dst + v * 32, make_float4(__uint_as_float(r[4 * v]),
+                                                                 __uint_as_float(r[4 * v + 1]),
+                                                                 __uint_as_float(r[4 * v + 2]),
+                                                                 __uint_as_float(r[4 * v + 3])));
+                        }
+                        continue;  // warp-uniform: w.split is the same on every lane
                     }
-                    if (w.split == 0 && row_live) {
+                    if (w.split == 0 && warp_live) {
                         // Owner: add the other splits' partials, in split order.
                         for (int sp = 1; sp < p.sk_splits; ++sp) {
                             const float4* src = reinterpret_cast<const float4*>(
                                 ws_tile + (long long)(sp - 1) * CG * kTileFloats + ws_off);
+                            float4 q[8];
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) q[v] = __ldcg(src + v * 32);
 #pragma unroll
                             for (int v = 0; v < 8; ++v) {
-                                const float4 q = __ldcg(src + v);
-                                r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q.x);
-                                r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q.y);
-                                r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q.z);
-                                r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q.w);
+                                r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q[v].x);
+                                r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q[v].y);
+                                r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q[v].z);
+                                r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q[v].w);
                             }
                         }
                     }
