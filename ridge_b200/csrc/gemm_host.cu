@@ -164,6 +164,22 @@ const KernelEntry* find_entry(const ridge_tile_config& c, int* index = nullptr) 
 
 int smem_for(const KernelEntry& e, int stages) { return e.fixed_smem + stages * e.stage_bytes; }
 
+// Dynamic shared memory a launch requests. When shared memory alone would let
+// more CTAs share an SM than Tensor Memory can hold, the request is padded so
+// the hardware never co-schedules a CTA whose tcgen05.alloc would have to
+// wait for another CTA to exit: split-K owners wait on other CTAs' partials,
+// so every CTA of the grid must be able to run at once.
+int launch_smem(const KernelEntry& e, int stages) {
+    int smem = e.fixed_smem + stages * e.stage_bytes;
+    const int by_tmem = kTmemColsPerSm / e.tmem_cols;
+    const int by_smem = kSmemPerSm / (smem + kSmemReservedPerCta);
+    if (by_smem > by_tmem) {
+        const int pad_to = kSmemPerSm / (by_tmem + 1) - kSmemReservedPerCta + 1;
+        smem = std::max(smem, pad_to);
+    }
+    return smem;
+}
+
 int ctas_per_sm(const KernelEntry& e, int stages) {
     const int by_smem = kSmemPerSm / (smem_for(e, stages) + kSmemReservedPerCta);
     const int by_tmem = kTmemColsPerSm / e.tmem_cols;
@@ -280,7 +296,7 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     if (!e) return RIDGE_EINVAL;
     plan->e = e;
     plan->idx = idx;
-    plan->smem = smem_for(*e, cfg.stages);
+    plan->smem = launch_smem(*e, cfg.stages);
     int st = ensure_smem_attr(*e, idx, dev);
     if (st != RIDGE_OK) return st;
     const int64_t tiles = ((M + e->BM - 1) / e->BM) * ((N + e->BN - 1) / e->BN);
