@@ -126,9 +126,10 @@ int ridge_gemm_workspace_size(const ridge_tile_config* cfg, int64_t M, int64_t N
 
 /*
  * ridge_gemm_launch with a caller-owned workspace of at least
- * ridge_gemm_workspace_size bytes (256-byte aligned). Its counter area must be
- * zero before the first launch (e.g. cudaMemset once); every launch leaves it
- * zero again. Launches that share one workspace must be ordered (one stream).
+ * ridge_gemm_workspace_size bytes (256-byte aligned). Its first 64 KB are the
+ * split-K counter area, which must be zero before the first launch (e.g.
+ * cudaMemset once); every launch leaves it zero again, so one workspace can
+ * serve any sequence of configs and shapes. Launches that share one workspace must be ordered (one stream).
  * ridge_gemm_launch itself keeps such a workspace per device and stream.
  */
 int ridge_gemm_launch_ws(const ridge_tile_config* cfg, const void* A, const void* B, void* C,

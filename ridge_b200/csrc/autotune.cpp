@@ -200,13 +200,19 @@ int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const i
                 e.status = ts;
                 e.measured_tflops = ts == RIDGE_OK ? 2.0 * M * N * K / (ms * 1e-3) / 1e12 : 0.0;
                 int32_t code = 0;
-                // A launch error or a device-side timeout is sticky for this
-                // device: stop this worker, the others keep going.
+                // A CUDA error is sticky for this device's context: stop this
+                // worker, the others keep going. A device-side timeout (bounded
+                // wait) leaves the context usable: record it, clear it, go on.
                 if (ts > 0) break;
-                if (ridge_device_error(1, &code) != RIDGE_OK || code != 0) {
-                    e.status = RIDGE_EDEVICE;
+                const int de = ridge_device_error(1, &code);
+                if (de != RIDGE_OK) {
+                    e.status = de;
                     e.measured_tflops = 0.0;
                     break;
+                }
+                if (code != 0) {
+                    e.status = RIDGE_EDEVICE;
+                    e.measured_tflops = 0.0;
                 }
             }
         }

@@ -35,6 +35,7 @@ constexpr int kMaxDynSmem = 232448;   // 227 KB opt-in limit per CTA on sm_100
 constexpr int kSmemPerSm = 233472;    // 228 KB per SM
 constexpr int kSmemReservedPerCta = 1024;
 constexpr int kTmemColsPerSm = 512;
+constexpr int64_t kCounterBytes = 64 * 1024;  // split-K counter area at the head of a workspace
 
 const std::vector<KernelEntry>& registry() {
     static const std::vector<KernelEntry> entries = [] {
@@ -317,9 +318,19 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     plan->sk_tiles = int(rem);
     plan->sk_splits = int(s);
     plan->grid_units = int(std::max<int64_t>(std::min(tiles, units), rem * s));
+    // Workspace: [counters: kCounterBytes][FP32 partial tiles]. The counter
+    // area sits at a fixed offset so that every config sharing a workspace
+    // finds it zeroed (owners reset their counters; partials never overlap it).
+    if (rem * e->cta_group * e->warps * 4 > kCounterBytes) {
+        plan->dp_tiles = int(tiles);
+        plan->sk_tiles = 0;
+        plan->sk_splits = 1;
+        plan->grid_units = int(std::min(tiles, units));
+        return RIDGE_OK;
+    }
     const size_t tile_floats = size_t(e->partial_floats);
-    plan->ws_partials = (size_t(rem) * (s - 1) * e->cta_group * tile_floats * 4 + 255) / 256 * 256;
-    plan->ws_bytes = plan->ws_partials + size_t(rem) * e->cta_group * e->warps * 4;
+    plan->ws_partials = size_t(rem) * (s - 1) * e->cta_group * tile_floats * 4;
+    plan->ws_bytes = kCounterBytes + plan->ws_partials;
     return RIDGE_OK;
 }
 
@@ -421,8 +432,8 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     p.dp_tiles = plan.dp_tiles;
     p.sk_tiles = plan.sk_tiles;
     p.sk_splits = plan.sk_splits;
-    p.workspace = static_cast<float*>(ws);
-    p.counters = ws ? reinterpret_cast<int*>(static_cast<char*>(ws) + plan.ws_partials) : nullptr;
+    p.counters = static_cast<int*>(ws);
+    p.workspace = ws ? reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes) : nullptr;
     cudaError_t ce = e->launch(&tmap_a, &tmap_b, &tmap_c, &p, plan.grid_units * e->cta_group,
                                plan.smem, stream);
     return int(ce);
@@ -546,6 +557,13 @@ int ridge_device_error(int clear, int32_t* code) {
     if (clear && v != 0) {
         e = cudaMemset(dev->err_word, 0, sizeof(int));
         if (e != cudaSuccess) return int(e);
+        // A kernel that gave up may have left split-K counters non-zero.
+        int device = 0;
+        cudaGetDevice(&device);
+        WorkspaceCache& c = g_ws[device];
+        std::lock_guard<std::mutex> lock(c.mu);
+        for (auto& kv : c.by_stream)
+            if (kv.second.first) cudaMemset(kv.second.first, 0, size_t(kCounterBytes));
     }
     return RIDGE_OK;
 }
