@@ -2,7 +2,7 @@
 
 The library is loaded from ridge_b200/lib/. There is no fallback: if the
 native library is missing, importing ridge_b200 raises ImportError telling the
-user to build it (python -m ridge_b200.build).
+user to build it (python ridge_b200/build.py).
 """
 
 from __future__ import annotations
@@ -119,7 +119,7 @@ def _load():
     if not LIB_PATH.exists():
         raise ImportError(
             "ridge_b200: native library %s is missing; build it with "
-            "`python -m ridge_b200.build` (there is no non-native fallback)" % LIB_PATH)
+            "`python ridge_b200/build.py` (there is no non-native fallback)" % LIB_PATH)
     lib = C.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | getattr(os, "RTLD_GLOBAL", 0))
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name, None)

@@ -6,7 +6,7 @@ g++-compatible host objects into one shared library that exports the C ABI
 declared in include/ridge_b200.h. Object files go to ridge_b200/_build/ and are
 rebuilt only when a source or header is newer than the object.
 
-Usage: python -m ridge_b200.build [-j N] [--verbose] [--ptxas-info]
+Usage: python ridge_b200/build.py [-j N] [--verbose] [--ptxas-info]
 """
 
 from __future__ import annotations
