@@ -28,6 +28,7 @@ extern "C" {
 #define RIDGE_ENOTSUP (-3)  /* device is not sm_100 / feature not built */
 #define RIDGE_EIO (-4)      /* file missing or unparseable */
 #define RIDGE_ERANGE (-5)   /* index out of range */
+#define RIDGE_ENOSCRATCH (-6) /* launch needs more scratch than ridge_gemm_launch_noalloc has */
 
 /* Human-readable text for any status returned by this library. */
 const char* ridge_status_string(int status);
@@ -135,6 +136,29 @@ int ridge_gemm_workspace_size(const ridge_tile_config* cfg, int64_t M, int64_t N
 int ridge_gemm_launch_ws(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
                          int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                          void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * ridge_gemm_launch for callers that must not allocate device memory (code
+ * running inside a pool or arena owned by its host framework, or on a path
+ * where cudaMalloc is forbidden because it synchronises the device). No
+ * counterpart in the reference. Instead of allocating a split-K workspace it
+ * uses one fixed scratch array inside this library's device image,
+ * ridge_gemm_noalloc_scratch_bytes() (16 MiB) on every GPU that loads the
+ * library, held until the process exits. A launch whose split-K tail would
+ * need more returns RIDGE_ENOSCRATCH (use ridge_gemm_launch or
+ * ridge_gemm_launch_ws, or a config with split_k = 1). The first call on a
+ * device resolves the array's device address and clears its counter area;
+ * make that first call before any stream capture. All calls on a device share
+ * the array, so calls that can overlap on the GPU (different streams without
+ * ordering) race; order them on one stream. Never allocates or frees memory.
+ */
+int ridge_gemm_launch_noalloc(const ridge_tile_config* cfg, const void* A, const void* B,
+                              void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                              int64_t ldc, void* stream);
+
+/* Size in bytes of ridge_gemm_launch_noalloc's fixed per-device scratch. No counterpart in
+ * the reference. */
+int64_t ridge_gemm_noalloc_scratch_bytes(void);
 
 /* Same, addressing the variant by its table index. */
 int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,

@@ -19,6 +19,7 @@ RIDGE_EDEVICE = -2
 RIDGE_ENOTSUP = -3
 RIDGE_EIO = -4
 RIDGE_ERANGE = -5
+RIDGE_ENOSCRATCH = -6
 
 BOTTLENECKS = ["TENSOR_CORE", "SMEM", "HBM", "OCC", "WAVES", "ENVELOPE", "DOES_NOT_FIT",
                "EPILOGUE", "L2"]
@@ -97,6 +98,9 @@ SIGNATURES = {
                                             C.POINTER(_i64)]),
     "ridge_gemm_launch_ws": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _vp, _i64, _vp]),
+    "ridge_gemm_launch_noalloc": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64,
+                                            _i64, _i64, _i64, _i64, _vp]),
+    "ridge_gemm_noalloc_scratch_bytes": (_i64, []),
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                             _i64, _i64, _vp]),
     "ridge_device_error": (C.c_int, [C.c_int, C.POINTER(_i32)]),

@@ -454,6 +454,8 @@ const char* ridge_status_string(int s) {
         case RIDGE_ENOTSUP: return "not supported on this device (needs sm_100)";
         case RIDGE_EIO: return "file missing or unparseable";
         case RIDGE_ERANGE: return "index out of range";
+        case RIDGE_ENOSCRATCH:
+            return "launch needs more split-K scratch than the fixed no-allocation array holds";
         default: break;
     }
     if (s > 0) return cudaGetErrorString(cudaError_t(s));
