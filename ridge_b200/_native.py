@@ -114,6 +114,14 @@ SIGNATURES = {
                                  C.POINTER(TuneEntryC), _i32]),
     "ridge_time_gemm": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _i32, _vp, C.POINTER(C.c_double)]),
+    "ridge_cal_umma": (C.c_int, [_i32, _i32, _i32, C.POINTER(C.c_double),
+                                 C.POINTER(C.c_double)]),
+    "ridge_cal_tma": (C.c_int, [_i64, _i32, _i32, _i32, C.POINTER(C.c_double),
+                                C.POINTER(C.c_double)]),
+    "ridge_cal_epi": (C.c_int, [_i32, C.POINTER(C.c_double)]),
+    "ridge_cal_copy": (C.c_int, [_i64, C.POINTER(C.c_double)]),
+    "ridge_cal_launch": (C.c_int, [C.POINTER(C.c_double)]),
+    "ridge_cal_clock": (C.c_int, [C.POINTER(C.c_double)]),
     "ridge_slab_bounds": (C.c_int, [_i64, _i32, _i32, _i64, C.POINTER(_i64), C.POINTER(_i64)]),
     "ridge_slabs_to_rowmajor": (C.c_int, [_vp, _vp, _i64, _i64, _i32, _i64, _i64, _vp]),
 }

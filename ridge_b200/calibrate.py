@@ -1,0 +1,179 @@
+"""Runs the sm_100a calibration microbenchmarks and writes the B200 hardware
+model (data/hardware/b200.json by default).
+
+Reference: bench/calibrate/run-calibration.py runs four CUDA binaries, parses
+their CAL_RESULT lines, checks each constant against a datasheet band and
+writes a flat JSON that HardwareModel::loadFromJson reads. Same contract here,
+with the microbenchmarks built into libridge_b200.so
+(include/ridge_b200_calibrate.h) and constants for the tcgen05/TMA kernel:
+
+  ummaCycles128x256  cycles per 128x256x16 tcgen05.mma (tensor issue rate)
+  ummaM64Ratio       cycles(64x256x16) / cycles(128x256x16)
+  smemBytesPerCycle  operand bytes/cycle/SM the tensor core reads from shared
+                     memory, from the MMA cycle count at small N
+  smemMmaOverlap     1 when those reads overlap the MMA (cycles = max), 0 when
+                     they add (cycles = sum); whichever fits the N sweep better
+  l2BytesPerSec      aggregate TMA fill rate from an L2-resident tensor
+  hbmBytesPerSec     aggregate TMA fill rate from a tensor 8x larger than L2
+  epiBytesPerCycleW4/W8  epilogue drain rate per SM with 4 / 8 warps
+  tmaLatencyCycles   load latency: bytes in flight / per-SM rate at depth 1
+  launchOverheadSec  back-to-back launch cost of an empty kernel
+  clockHz            SM clock measured under full tensor load
+
+Usage: python -m ridge_b200.calibrate [--out data/hardware/b200.json]
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import sys
+import time
+from pathlib import Path
+
+from ._native import check, lib
+
+ROOT = Path(__file__).resolve().parent.parent
+
+# Datasheet-derived sanity bands (run-calibration.py:113-126 in the reference):
+# a constant outside its band means the benchmark, not the chip, is wrong.
+BANDS = {
+    "ummaCycles128x256": (100.0, 200.0),   # 128 nominal (8192 FLOP/cycle/SM)
+    "smemBytesPerCycle": (64.0, 512.0),
+    "l2BytesPerSec": (4e12, 40e12),
+    "hbmBytesPerSec": (3e12, 8.5e12),
+    "clockHz": (0.8e9, 2.1e9),
+}
+
+
+def umma(m, n, iters=20000):
+    cyc, hz = C.c_double(), C.c_double()
+    check(lib.ridge_cal_umma(m, n, iters, C.byref(cyc), C.byref(hz)), "ridge_cal_umma")
+    return cyc.value, hz.value
+
+
+def tma(tensor_bytes, box_rows, depth, ctas=1):
+    per_sm, total = C.c_double(), C.c_double()
+    check(lib.ridge_cal_tma(tensor_bytes, box_rows, depth, ctas, C.byref(per_sm), C.byref(total)),
+          "ridge_cal_tma")
+    return per_sm.value, total.value
+
+
+def epi(warps):
+    v = C.c_double()
+    check(lib.ridge_cal_epi(warps, C.byref(v)), "ridge_cal_epi")
+    return v.value
+
+
+def copy_bw(nbytes=1 << 31):
+    v = C.c_double()
+    check(lib.ridge_cal_copy(nbytes, C.byref(v)), "ridge_cal_copy")
+    return v.value
+
+
+def launch_overhead():
+    v = C.c_double()
+    check(lib.ridge_cal_launch(C.byref(v)), "ridge_cal_launch")
+    return v.value
+
+
+def fit_smem(cycles_by_n, m=128):
+    """From cycles(n) of m x n x 16 MMAs: tensor cycles per 128x256 MMA, smem
+    bytes/cycle, and whether operand reads overlap (max) or add (sum).
+    Operand bytes per MMA: (m + n) * 16 * 2."""
+    c256 = cycles_by_n[256]
+    best = None
+    for overlap in (1, 0):
+        # the tensor part scales with n; solve the smem rate from the smallest n
+        n0 = min(cycles_by_n)
+        bytes0 = (m + n0) * 32
+        t0 = c256 * n0 / 256.0
+        if overlap:
+            bw = bytes0 / cycles_by_n[n0] if cycles_by_n[n0] > t0 * 1.02 else 1e9
+        else:
+            extra = cycles_by_n[n0] - t0
+            bw = bytes0 / extra if extra > 1e-6 else 1e9
+        err = 0.0
+        for n, c in cycles_by_n.items():
+            t = c256 * n / 256.0
+            s = (m + n) * 32 / bw
+            pred = max(t, s) if overlap else t + s
+            err += abs(pred - c) / c
+        if best is None or err < best[0]:
+            best = (err, overlap, bw)
+    _, overlap, bw = best
+    return c256, min(bw, 1024.0), float(overlap)
+
+
+def calibrate(verbose=True):
+    log = (lambda *a: print(*a, flush=True)) if verbose else (lambda *a: None)
+    res, raw = {}, {}
+    cyc = {}
+    for n in (64, 128, 256):
+        cyc[n], hz = umma(128, n)
+        raw["umma_128x%d" % n] = cyc[n]
+        log("umma 128x%dx16: %.2f cycles (clock %.0f MHz)" % (n, cyc[n], hz / 1e6))
+    c64, _ = umma(64, 256)
+    raw["umma_64x256"] = c64
+    c256, hz = umma(128, 256, 40000)
+    cyc[256] = c256
+    res["clockHz"] = hz
+    res["ummaCycles128x256"], res["smemBytesPerCycle"], res["smemMmaOverlap"] = fit_smem(cyc)
+    res["ummaM64Ratio"] = c64 / c256
+    log("m64 ratio %.3f, smem %.1f B/cycle, overlap %d" % (
+        res["ummaM64Ratio"], res["smemBytesPerCycle"], res["smemMmaOverlap"]))
+    # TMA fill: L2-resident (32 MB tensor) vs HBM-streaming (8 GB) at deep rings.
+    l2_best, hbm_best = 0.0, 0.0
+    for box, depth in ((256, 6), (128, 12), (256, 3)):
+        per_sm, tot = tma(32 << 20, box, depth)
+        raw["tma_l2_box%d_d%d" % (box, depth)] = [per_sm, tot]
+        l2_best = max(l2_best, tot)
+        log("tma L2  box %3d depth %2d: %.1f B/cycle/SM  %.2f TB/s" % (box, depth, per_sm, tot / 1e12))
+    for box, depth in ((256, 6), (128, 12)):
+        per_sm, tot = tma(8 << 30, box, depth)
+        raw["tma_hbm_box%d_d%d" % (box, depth)] = [per_sm, tot]
+        hbm_best = max(hbm_best, tot)
+        log("tma HBM box %3d depth %2d: %.1f B/cycle/SM  %.2f TB/s" % (box, depth, per_sm, tot / 1e12))
+    res["l2BytesPerSec"] = l2_best
+    res["hbmBytesPerSec"] = hbm_best
+    # latency: one box in flight per SM
+    per_sm1, _ = tma(32 << 20, 128, 1)
+    res["tmaLatencyCycles"] = 128 * 128 / per_sm1
+    raw["tma_l2_box128_d1"] = per_sm1
+    log("tma latency (depth 1): %.0f cycles" % res["tmaLatencyCycles"])
+    res["epiBytesPerCycleW4"] = epi(4)
+    res["epiBytesPerCycleW8"] = epi(8)
+    log("epilogue: %.1f / %.1f B/cycle/SM (4 / 8 warps)" % (res["epiBytesPerCycleW4"],
+                                                           res["epiBytesPerCycleW8"]))
+    raw["copy_bytes_per_sec"] = copy_bw()
+    res["launchOverheadSec"] = launch_overhead()
+    log("copy %.2f TB/s, launch %.2f us" % (raw["copy_bytes_per_sec"] / 1e12,
+                                           res["launchOverheadSec"] * 1e6))
+    res.update({"numSMs": 148, "l2Bytes": 126.0 * 1024 * 1024, "smemBytesPerSM": 233472,
+                "tmemColsPerSM": 512, "maxCtasPerSM": 32})
+    bad = {k: v for k, v in res.items() if k in BANDS and not BANDS[k][0] <= v <= BANDS[k][1]}
+    return res, raw, bad
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=str(ROOT / "data" / "hardware" / "b200.json"))
+    a = ap.parse_args(argv)
+    res, raw, bad = calibrate()
+    if bad:
+        print("constants outside their datasheet bands, not written: %s" % bad, file=sys.stderr)
+        return 1
+    import torch
+    name = torch.cuda.get_device_name()
+    doc = {"name": name, "note": "measured by ridge_b200.calibrate (sm_100a microbenchmarks) on %s"
+           % time.strftime("%Y-%m-%d"), **res}
+    Path(a.out).parent.mkdir(parents=True, exist_ok=True)
+    Path(a.out).write_text(json.dumps(doc, indent=1) + "\n")
+    Path(a.out).with_suffix(".raw.json").write_text(json.dumps(raw, indent=1) + "\n")
+    print("wrote", a.out)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,472 @@
+// sm_100a calibration microbenchmarks for the B200 cost model.
+//
+// Reference: bench/calibrate/cal-*.cu measured the A100 model's constants
+// (mma.sync issue rate, ldmatrix shared-memory bandwidth, HBM read bandwidth,
+// warps needed to hide latency). On B200 the kernel's resources are different,
+// so each benchmark here measures what the GEMM family actually uses:
+//
+//   ridge_cal_umma   cycles per tcgen05.mma (kind::f16) for one SM, per UMMA
+//                    shape (M 64/128, N 64..256), both operands in shared
+//                    memory: tensor issue rate, and -- through the N
+//                    dependence -- the shared-memory operand feed and whether
+//                    it overlaps the MMA or adds to it.
+//   ridge_cal_tma    TMA tile-load bandwidth per SM and in aggregate, as a
+//                    function of bytes kept in flight (ring depth x box), from
+//                    an L2-resident tensor or an HBM-streaming one: the L2 and
+//                    HBM fill ceilings and the load latency (Little's law).
+//   ridge_cal_epi    the epilogue drain: TMEM -> registers -> FP16 -> swizzled
+//                    shared memory -> TMA store, with 4 or 8 warps per SM.
+//   ridge_cal_copy   HBM copy bandwidth (read + write).
+//   ridge_cal_launch fixed cost of one kernel launch between two events.
+//
+// Every kernel runs one CTA per SM, times itself with the SM clock, and every
+// wait in it is bounded (RIDGE_WAIT_LIMIT_NS) so a broken run reports an error
+// instead of hanging.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "../../include/ridge_b200_calibrate.h"
+#include "../../include/ridge_b200.h"
+#include "ptx_sm100.cuh"
+
+namespace ridge_b200 {
+namespace {
+
+__device__ __forceinline__ unsigned long long clk() {
+    unsigned long long c;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+    return c;
+}
+
+// ------------------------------------------------------------------ UMMA
+
+// One thread issues `iters` tcgen05.mma of shape (m, n, 16) alternating
+// between two TMEM accumulators and four K offsets inside one 128B-swizzled
+// operand tile, then waits for completion through tcgen05.commit.
+__global__ void cal_umma_kernel(int m, int n, int iters, unsigned long long* cycles, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* p = smem_raw + (base - raw);
+    // A: 128 x 64 FP16 (16 KB); B: 256 x 64 FP16 (32 KB); zeros.
+    for (int i = threadIdx.x; i < (48 * 1024) / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(p)[i] = make_uint4(0, 0, 0, 0);
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tmem_slot;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_barrier_init();
+    }
+    fence_proxy_async_smem();
+    if (warp == 0) {
+        tmem_alloc<1>(smem_u32(&tmem_slot), 512);
+        tmem_relinquish<1>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    if (threadIdx.x == 0) {
+        const uint32_t idesc = make_idesc_f16_f32(m, n);
+        const unsigned long long t0 = clk();
+        for (int i = 0; i < iters; ++i) {
+            const int kk = i & 3;
+            const uint64_t ad = make_smem_desc<128>(base + kk * 32);
+            const uint64_t bd = make_smem_desc<128>(base + 16384 + kk * 32);
+            umma_f16<1>(tmem + uint32_t((i & 1) * 256), ad, bd, idesc, 1u);
+        }
+        umma_commit(smem_u32(&bar));
+        mbar_wait(smem_u32(&bar), 0, nullptr, err, kErrTimeoutMma);
+        const unsigned long long t1 = clk();
+        cycles[blockIdx.x] = t1 - t0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc<1>(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------ TMA
+
+// One producer thread per CTA keeps `depth` box loads in flight over a ring:
+// load i goes to slot i % depth after the slot's previous load has landed.
+// CTA b reads rows starting at (b * rows_step) mod rows_total, walking K, so
+// an L2-resident tensor is shared by all SMs while a large one streams.
+__global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int depth, int box_bytes,
+                               int loads, int box_rows, int k_boxes, int row_tiles,
+                               unsigned long long* cycles, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    __shared__ uint64_t bars[16];
+    if (threadIdx.x != 0) return;
+    for (int s = 0; s < depth; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    fence_barrier_init();
+    const unsigned long long t0 = clk();
+    for (int i = 0; i < loads; ++i) {
+        const int s = i % depth;
+        const uint32_t b = smem_u32(&bars[s]);
+        if (i >= depth && !mbar_wait(b, uint32_t((i / depth - 1) & 1), nullptr, err, kErrTimeoutProducer))
+            break;
+        mbar_arrive_expect_tx(b, uint32_t(box_bytes));
+        const int g = int(blockIdx.x) * loads + i;
+        const int kx = (g % k_boxes) * 64;
+        const int ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
+        tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
+    }
+    for (int i = std::max(0, loads - depth); i < loads; ++i)
+        mbar_wait(smem_u32(&bars[i % depth]), uint32_t((i / depth) & 1), nullptr, err,
+                  kErrTimeoutDrain);
+    cycles[blockIdx.x] = clk() - t0;
+}
+
+// ------------------------------------------------------------------ epilogue
+
+// `warps` warps drain 32 x 32 FP32 chunks from TMEM, convert to FP16, stage
+// them 64B-swizzled in shared memory and TMA-store them to C, the same
+// sequence as the GEMM epilogue; `chunks` chunks per warp.
+__global__ void cal_epi_kernel(const __grid_constant__ CUtensorMap cmap, int chunks, int n_tiles,
+                               unsigned long long* cycles) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    __shared__ uint32_t tmem_slot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+        tmem_alloc<1>(smem_u32(&tmem_slot), 256);
+        tmem_relinquish<1>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const int quad = warp & 3;
+    const uint32_t buf0 = base + uint32_t(warp * 2 * 2048);
+    const unsigned long long t0 = clk();
+    int buf = 0;
+    for (int c = 0; c < chunks; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + (uint32_t(quad * 32) << 16) + uint32_t((c % 8) * 32), r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            __half2 h = __floats2half2_rn(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+            pk[e] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        const uint32_t sb = buf0 + uint32_t(buf * 2048);
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        const uint32_t row = sb + uint32_t(lane * 64), sw = uint32_t((lane >> 1) & 3);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + ((uint32_t(q) ^ sw) << 4)),
+                         "r"(pk[4 * q]), "r"(pk[4 * q + 1]), "r"(pk[4 * q + 2]), "r"(pk[4 * q + 3])
+                         : "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            const int t = (int(blockIdx.x) * 64 + warp * chunks + c) % n_tiles;
+            tma_store_2d(&cmap, sb, (t % 64) * 32, (t / 64) * 32);
+            tma_store_commit();
+        }
+        buf ^= 1;
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+    const unsigned long long t1 = clk();
+    if (lane == 0) atomicMax(cycles + blockIdx.x, t1 - t0);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc<1>(tmem, 256);
+    }
+}
+
+// ------------------------------------------------------------------ copy / launch
+
+__global__ void cal_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += size_t(gridDim.x) * blockDim.x)
+        dst[i] = src[i];
+}
+
+__global__ void cal_empty_kernel() {}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+int sm_count(int* n) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(n, cudaDevAttrMultiProcessorCount, dev);
+    return int(e);
+}
+
+int* err_word() {
+    static int* p = nullptr;
+    if (!p) cudaMalloc(&p, sizeof(int));
+    if (p) cudaMemset(p, 0, sizeof(int));
+    return p;
+}
+
+double median_cycles(const std::vector<unsigned long long>& v) {
+    std::vector<unsigned long long> s(v);
+    std::sort(s.begin(), s.end());
+    return s.empty() ? 0.0 : double(s[s.size() / 2]);
+}
+
+}  // namespace
+}  // namespace ridge_b200
+
+using namespace ridge_b200;
+
+extern "C" {
+
+int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, double* clock_hz) {
+    if (!cycles_per_mma || !(m == 64 || m == 128) || n < 16 || n > 256 || n % 16 || iters <= 0)
+        return RIDGE_EINVAL;
+    int sms = 0;
+    int st = sm_count(&sms);
+    if (st) return st;
+    unsigned long long* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, sizeof(unsigned long long) * sms);
+    if (e != cudaSuccess) return int(e);
+    int* err = err_word();
+    const int smem = 48 * 1024 + 1024;
+    cudaFuncSetAttribute(cal_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // Repeat until the clocks have settled under tensor load (about 0.3 s), and
+    // time the last launch with events as well as with the SM clock.
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    float ms = 0.f, spent = 0.f;
+    for (int r = 0; r < 200 && (r < 3 || spent < 300.f); ++r) {
+        cudaEventRecord(e0);
+        cal_umma_kernel<<<sms, 128, smem>>>(m, n, iters, d, err);
+        cudaEventRecord(e1);
+        if (cudaEventSynchronize(e1) != cudaSuccess) break;
+        cudaEventElapsedTime(&ms, e0, e1);
+        spent += ms;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    e = cudaDeviceSynchronize();
+    std::vector<unsigned long long> h(sms);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
+    int code = 0;
+    if (e == cudaSuccess) cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return int(e);
+    if (code) return RIDGE_EDEVICE;
+    *cycles_per_mma = median_cycles(h) / iters;
+    if (clock_hz) *clock_hz = median_cycles(h) / (double(ms) * 1e-3);
+    return RIDGE_OK;
+}
+
+int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t ctas_per_sm,
+                  double* bytes_per_cycle_sm, double* total_bytes_per_sec) {
+    if (!bytes_per_cycle_sm || !total_bytes_per_sec || depth < 1 || depth > 16 ||
+        !(box_rows == 64 || box_rows == 128 || box_rows == 256) || ctas_per_sm < 1 ||
+        tensor_bytes < (1 << 20))
+        return RIDGE_EINVAL;
+    auto enc = encoder();
+    if (!enc) return RIDGE_ENOTSUP;
+    int sms = 0;
+    int st = sm_count(&sms);
+    if (st) return st;
+    // Tensor: rows x 8192 FP16 (16 KB rows), K-major, box box_rows x 64 (128B swizzle).
+    const int64_t kcols = 8192;
+    const int64_t rows = std::max<int64_t>(box_rows, tensor_bytes / (kcols * 2) / box_rows * box_rows);
+    void* buf = nullptr;
+    cudaError_t e = cudaMalloc(&buf, size_t(rows * kcols * 2));
+    if (e != cudaSuccess) return int(e);
+    cudaMemset(buf, 0, size_t(rows * kcols * 2));
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(kcols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(kcols * 2)};
+    cuuint32_t box[2] = {64, cuuint32_t(box_rows)};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        cudaFree(buf);
+        return RIDGE_EINVAL;
+    }
+    const int box_bytes = box_rows * 128;
+    if (depth * box_bytes + 1024 > 232448 || ctas_per_sm * (depth * box_bytes + 2048) > 233472) {
+        cudaFree(buf);
+        return RIDGE_EINVAL;
+    }
+    const int grid = sms * ctas_per_sm;
+    // Each CTA moves ~16 MB (or the whole tensor once, spread over the grid,
+    // when it is larger than L2), after one untimed warm pass.
+    const int64_t per_cta = std::max<int64_t>(int64_t(16) << 20, rows * kcols * 2 / grid);
+    const int loads = int(std::min<int64_t>(per_cta / box_bytes, 1 << 20));
+    unsigned long long* d = nullptr;
+    e = cudaMalloc(&d, sizeof(unsigned long long) * grid);
+    int* err = err_word();
+    const int smem = depth * box_bytes + 1024;
+    cudaFuncSetAttribute(cal_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    const int k_boxes = int(kcols / 64), row_tiles = int(rows / box_rows);
+    cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, std::min(loads, 64), box_rows,
+                                       k_boxes, row_tiles, d, err);
+    cudaEventRecord(e0);
+    cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, loads, box_rows, k_boxes,
+                                       row_tiles, d, err);
+    cudaEventRecord(e1);
+    e = cudaDeviceSynchronize();
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    std::vector<unsigned long long> h(grid);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, sizeof(unsigned long long) * grid, cudaMemcpyDeviceToHost);
+    int code = 0;
+    if (e == cudaSuccess) cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(d);
+    cudaFree(buf);
+    if (e != cudaSuccess) return int(e);
+    if (code) return RIDGE_EDEVICE;
+    // Per SM: all CTAs on an SM together.
+    *bytes_per_cycle_sm = double(loads) * box_bytes * ctas_per_sm / median_cycles(h);
+    *total_bytes_per_sec = double(loads) * box_bytes * grid / (double(ms) * 1e-3);
+    return RIDGE_OK;
+}
+
+int ridge_cal_epi(int32_t warps, double* bytes_per_cycle_sm) {
+    if (!bytes_per_cycle_sm || !(warps == 4 || warps == 8)) return RIDGE_EINVAL;
+    auto enc = encoder();
+    if (!enc) return RIDGE_ENOTSUP;
+    int sms = 0;
+    int st = sm_count(&sms);
+    if (st) return st;
+    // C: 8192 x 2048 FP16 (32 MB), stored in 32 x 32 chunks.
+    const int64_t rows = 8192, cols = 2048;
+    void* c = nullptr;
+    cudaError_t e = cudaMalloc(&c, size_t(rows * cols * 2));
+    if (e != cudaSuccess) return int(e);
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(cols * 2)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, c, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        cudaFree(c);
+        return RIDGE_EINVAL;
+    }
+    unsigned long long* d = nullptr;
+    cudaMalloc(&d, sizeof(unsigned long long) * sms);
+    cudaMemset(d, 0, sizeof(unsigned long long) * sms);
+    const int chunks = 2048;
+    const int smem = warps * 2 * 2048 + 1024;
+    const int n_tiles = int((rows / 32) * (cols / 32));
+    cudaFuncSetAttribute(cal_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cal_epi_kernel<<<sms, warps * 32, smem>>>(map, 64, n_tiles, d);
+    cudaMemset(d, 0, sizeof(unsigned long long) * sms);
+    cal_epi_kernel<<<sms, warps * 32, smem>>>(map, chunks, n_tiles, d);
+    e = cudaDeviceSynchronize();
+    std::vector<unsigned long long> h(sms);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    cudaFree(c);
+    if (e != cudaSuccess) return int(e);
+    *bytes_per_cycle_sm = double(chunks) * warps * 2048 / median_cycles(h);
+    return RIDGE_OK;
+}
+
+int ridge_cal_copy(int64_t bytes, double* bytes_per_sec) {
+    if (!bytes_per_sec || bytes < (1 << 24)) return RIDGE_EINVAL;
+    int sms = 0;
+    int st = sm_count(&sms);
+    if (st) return st;
+    void *a = nullptr, *b = nullptr;
+    cudaError_t e = cudaMalloc(&a, size_t(bytes));
+    if (e != cudaSuccess) return int(e);
+    e = cudaMalloc(&b, size_t(bytes));
+    if (e != cudaSuccess) {
+        cudaFree(a);
+        return int(e);
+    }
+    cudaMemset(a, 0, size_t(bytes));
+    const size_t n = size_t(bytes) / 16;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    float best = 1e30f;
+    for (int r = 0; r < 6; ++r) {
+        cudaEventRecord(e0);
+        cal_copy_kernel<<<sms * 8, 512>>>(static_cast<uint4*>(a), static_cast<uint4*>(b), n);
+        cudaEventRecord(e1);
+        cudaEventSynchronize(e1);
+        float ms = 0;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (r > 0) best = std::min(best, ms);
+    }
+    e = cudaGetLastError();
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(a);
+    cudaFree(b);
+    if (e != cudaSuccess) return int(e);
+    *bytes_per_sec = 2.0 * double(bytes) / (double(best) * 1e-3);
+    return RIDGE_OK;
+}
+
+int ridge_cal_launch(double* seconds) {
+    if (!seconds) return RIDGE_EINVAL;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    for (int i = 0; i < 10; ++i) cal_empty_kernel<<<148, 128>>>();
+    const int n = 200;
+    cudaEventRecord(e0);
+    for (int i = 0; i < n; ++i) cal_empty_kernel<<<148, 128>>>();
+    cudaEventRecord(e1);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return int(e);
+    *seconds = double(ms) * 1e-3 / n;
+    return RIDGE_OK;
+}
+
+int ridge_cal_clock(double* hz) {
+    if (!hz) return RIDGE_EINVAL;
+    int dev = 0, khz = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev);
+    if (e != cudaSuccess) return int(e);
+    *hz = double(khz) * 1e3;
+    return RIDGE_OK;
+}
+
+}  // extern "C"
