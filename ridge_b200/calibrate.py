@@ -137,10 +137,14 @@ def calibrate(verbose=True):
         log("tma HBM box %3d depth %2d: %.1f B/cycle/SM  %.2f TB/s" % (box, depth, per_sm, tot / 1e12))
     res["l2BytesPerSec"] = l2_best
     res["hbmBytesPerSec"] = hbm_best
-    # latency: one box in flight per SM
-    per_sm1, _ = tma(32 << 20, 128, 1)
-    res["tmaLatencyCycles"] = 128 * 128 / per_sm1
-    raw["tma_l2_box128_d1"] = per_sm1
+    # latency: fill rate against bytes in flight (one box per ring slot)
+    curve = {}
+    for depth in (1, 2, 4, 8):
+        per_sm, tot = tma(32 << 20, 128, depth)
+        curve[depth] = per_sm
+        log("tma L2  box 128 depth %2d: %.1f B/cycle/SM  %.2f TB/s" % (depth, per_sm, tot / 1e12))
+    raw["tma_l2_box128_depth_curve"] = curve
+    res["tmaLatencyCycles"] = 128 * 128 / curve[1]
     log("tma latency (depth 1): %.0f cycles" % res["tmaLatencyCycles"])
     res["epiBytesPerCycleW4"] = epi(4)
     res["epiBytesPerCycleW8"] = epi(8)

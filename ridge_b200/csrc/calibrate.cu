@@ -255,7 +255,11 @@ int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, 
     if (e != cudaSuccess) return int(e);
     int* err = err_word();
     const int smem = 48 * 1024 + 1024;
-    cudaFuncSetAttribute(cal_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(cal_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return int(e);
+    }
     // Repeat until the clocks have settled under tensor load (about 0.3 s), and
     // time the last launch with events as well as with the SM clock.
     cudaEvent_t e0, e1;
@@ -266,13 +270,15 @@ int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, 
         cudaEventRecord(e0);
         cal_umma_kernel<<<sms, 128, smem>>>(m, n, iters, d, err);
         cudaEventRecord(e1);
+        if (cudaPeekAtLastError() != cudaSuccess) break;
         if (cudaEventSynchronize(e1) != cudaSuccess) break;
         cudaEventElapsedTime(&ms, e0, e1);
         spent += ms;
     }
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
-    e = cudaDeviceSynchronize();
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     std::vector<unsigned long long> h(sms);
     if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
     int code = 0;
@@ -328,7 +334,12 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     e = cudaMalloc(&d, sizeof(unsigned long long) * grid);
     int* err = err_word();
     const int smem = depth * box_bytes + 1024;
-    cudaFuncSetAttribute(cal_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    e = cudaFuncSetAttribute(cal_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        cudaFree(buf);
+        return int(e);
+    }
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
@@ -339,7 +350,8 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, loads, box_rows, k_boxes,
                                        row_tiles, d, err);
     cudaEventRecord(e1);
-    e = cudaDeviceSynchronize();
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     float ms = 0;
     cudaEventElapsedTime(&ms, e0, e1);
     std::vector<unsigned long long> h(grid);
@@ -391,7 +403,8 @@ int ridge_cal_epi(int32_t warps, double* bytes_per_cycle_sm) {
     cal_epi_kernel<<<sms, warps * 32, smem>>>(map, 64, n_tiles, d);
     cudaMemset(d, 0, sizeof(unsigned long long) * sms);
     cal_epi_kernel<<<sms, warps * 32, smem>>>(map, chunks, n_tiles, d);
-    e = cudaDeviceSynchronize();
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     std::vector<unsigned long long> h(sms);
     if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, sizeof(unsigned long long) * sms, cudaMemcpyDeviceToHost);
     cudaFree(d);
