@@ -53,9 +53,10 @@ def umma(m, n, iters=20000):
     return cyc.value, hz.value
 
 
-def tma(tensor_bytes, box_rows, depth, ctas=1):
+def tma(tensor_bytes, box_rows, depth, ctas=1, private=0, issuers=1):
     per_sm, total = C.c_double(), C.c_double()
-    check(lib.ridge_cal_tma(tensor_bytes, box_rows, depth, ctas, C.byref(per_sm), C.byref(total)),
+    check(lib.ridge_cal_tma(tensor_bytes, box_rows, depth, ctas, private, issuers, C.byref(per_sm),
+                            C.byref(total)),
           "ridge_cal_tma")
     return per_sm.value, total.value
 
@@ -137,6 +138,25 @@ def calibrate(verbose=True):
         log("tma HBM box %3d depth %2d: %.1f B/cycle/SM  %.2f TB/s" % (box, depth, per_sm, tot / 1e12))
     res["l2BytesPerSec"] = l2_best
     res["hbmBytesPerSec"] = hbm_best
+    # the same loads, but no two SMs ever read the same bytes (76-96 MB, in L2)
+    for box, depth, tb in ((256, 6, 80 << 20), (128, 8, 96 << 20), (64, 12, 96 << 20)):
+        per_sm, tot = tma(tb, box, depth, 1, 1)
+        raw["tma_l2_private_box%d_d%d" % (box, depth)] = [per_sm, tot]
+        log("tma L2 private box %3d depth %2d: %.1f B/cycle/SM  %.2f TB/s" % (box, depth, per_sm,
+                                                                             tot / 1e12))
+    # several issuing threads in one CTA
+    for iss in (2, 4):
+        per_sm, tot = tma(32 << 20, 128, 8 // iss, 1, 0, iss)
+        raw["tma_l2_box128_issuers%d" % iss] = [per_sm, tot]
+        log("tma L2  box 128 depth %d, %d issuers: %.1f B/cycle/SM  %.2f TB/s" % (8 // iss, iss, per_sm,
+                                                                                tot / 1e12))
+    per_sm, tot = tma(8 << 30, 128, 2, 1, 0, 4)
+    raw["tma_hbm_box128_d2_issuers4"] = [per_sm, tot]
+    log("tma HBM box 128 depth  2, 4 issuers: %.1f B/cycle/SM  %.2f TB/s" % (per_sm, tot / 1e12))
+    # two CTAs per SM, shared boxes
+    per_sm, tot = tma(32 << 20, 128, 6, 2)
+    raw["tma_l2_box128_d6_2cta"] = [per_sm, tot]
+    log("tma L2  box 128 depth  6, 2 CTAs/SM: %.1f B/cycle/SM  %.2f TB/s" % (per_sm, tot / 1e12))
     # latency: fill rate against bytes in flight (one box per ring slot)
     curve = {}
     for depth in (1, 2, 4, 8):

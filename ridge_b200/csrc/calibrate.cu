@@ -103,31 +103,47 @@ __global__ void cal_umma_kernel(int m, int n, int iters, unsigned long long* cyc
 // CTA b reads rows starting at (b * rows_step) mod rows_total, walking K, so
 // an L2-resident tensor is shared by all SMs while a large one streams.
 __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int depth, int box_bytes,
-                               int loads, int box_rows, int k_boxes, int row_tiles,
-                               unsigned long long* cycles, int* err) {
+                               int loads, int box_rows, int k_boxes, int row_tiles, int private_regions,
+                               int issuers, unsigned long long* cycles, int* err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     __shared__ uint64_t bars[16];
-    if (threadIdx.x != 0) return;
-    for (int s = 0; s < depth; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    const int lane = threadIdx.x;
+    if (lane >= issuers) return;
+    // Issuer `lane` owns ring slots [lane * depth, (lane + 1) * depth) and
+    // loads lane, lane + issuers, ...
+    for (int s = 0; s < depth; ++s) mbar_init(smem_u32(&bars[lane * depth + s]), 1);
     fence_barrier_init();
+    __syncwarp((1u << issuers) - 1u);
     const unsigned long long t0 = clk();
-    for (int i = 0; i < loads; ++i) {
-        const int s = i % depth;
+    const int mine = loads / issuers;
+    for (int j = 0; j < mine; ++j) {
+        const int i = j * issuers + lane;
+        const int s = lane * depth + j % depth;
         const uint32_t b = smem_u32(&bars[s]);
-        if (i >= depth && !mbar_wait(b, uint32_t((i / depth - 1) & 1), nullptr, err, kErrTimeoutProducer))
+        if (j >= depth && !mbar_wait(b, uint32_t((j / depth - 1) & 1), nullptr, err, kErrTimeoutProducer))
             break;
         mbar_arrive_expect_tx(b, uint32_t(box_bytes));
-        const int g = int(blockIdx.x) * loads + i;
-        const int kx = (g % k_boxes) * 64;
-        const int ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
+        int kx, ry;
+        if (private_regions) {
+            // CTA b cycles over its own 16 boxes: row tile b % row_tiles, K
+            // segment b / row_tiles (no two CTAs read the same bytes).
+            const int seg = int(blockIdx.x) / row_tiles;
+            kx = ((seg * 16 + (i & 15)) % k_boxes) * 64;
+            ry = (int(blockIdx.x) % row_tiles) * box_rows;
+        } else {
+            const int g = int(blockIdx.x) * loads + i;
+            kx = (g % k_boxes) * 64;
+            ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
+        }
         tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
     }
-    for (int i = std::max(0, loads - depth); i < loads; ++i)
-        mbar_wait(smem_u32(&bars[i % depth]), uint32_t((i / depth) & 1), nullptr, err,
-                  kErrTimeoutDrain);
-    cycles[blockIdx.x] = clk() - t0;
+    for (int j = std::max(0, mine - depth); j < mine; ++j)
+        mbar_wait(smem_u32(&bars[lane * depth + j % depth]), uint32_t((j / depth) & 1), nullptr,
+                  err, kErrTimeoutDrain);
+    __syncwarp((1u << issuers) - 1u);
+    if (lane == 0) cycles[blockIdx.x] = clk() - t0;
 }
 
 // ------------------------------------------------------------------ epilogue
@@ -292,8 +308,10 @@ int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, 
 }
 
 int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t ctas_per_sm,
-                  double* bytes_per_cycle_sm, double* total_bytes_per_sec) {
-    if (!bytes_per_cycle_sm || !total_bytes_per_sec || depth < 1 || depth > 16 ||
+                  int32_t private_regions, int32_t issuers, double* bytes_per_cycle_sm,
+                  double* total_bytes_per_sec) {
+    if (!bytes_per_cycle_sm || !total_bytes_per_sec || depth < 1 || issuers < 1 ||
+        issuers * depth > 16 ||
         !(box_rows == 64 || box_rows == 128 || box_rows == 256) || ctas_per_sm < 1 ||
         tensor_bytes < (1 << 20))
         return RIDGE_EINVAL;
@@ -321,7 +339,8 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
         return RIDGE_EINVAL;
     }
     const int box_bytes = box_rows * 128;
-    if (depth * box_bytes + 1024 > 232448 || ctas_per_sm * (depth * box_bytes + 2048) > 233472) {
+    const int slots = depth * issuers;
+    if (slots * box_bytes + 1024 > 232448 || ctas_per_sm * (slots * box_bytes + 2048) > 233472) {
         cudaFree(buf);
         return RIDGE_EINVAL;
     }
@@ -329,11 +348,11 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     // Each CTA moves ~16 MB (or the whole tensor once, spread over the grid,
     // when it is larger than L2), after one untimed warm pass.
     const int64_t per_cta = std::max<int64_t>(int64_t(16) << 20, rows * kcols * 2 / grid);
-    const int loads = int(std::min<int64_t>(per_cta / box_bytes, 1 << 20));
+    const int loads = int(std::min<int64_t>(per_cta / box_bytes, 1 << 20)) / issuers * issuers;
     unsigned long long* d = nullptr;
     e = cudaMalloc(&d, sizeof(unsigned long long) * grid);
     int* err = err_word();
-    const int smem = depth * box_bytes + 1024;
+    const int smem = slots * box_bytes + 1024;
     e = cudaFuncSetAttribute(cal_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
         cudaFree(d);
@@ -344,11 +363,17 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     const int k_boxes = int(kcols / 64), row_tiles = int(rows / box_rows);
-    cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, std::min(loads, 64), box_rows,
-                                       k_boxes, row_tiles, d, err);
+    if (private_regions && int64_t(row_tiles) * (k_boxes / 16) < grid) {
+        cudaFree(d);
+        cudaFree(buf);
+        return RIDGE_EINVAL;  // tensor too small for one private region per CTA
+    }
+    cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, std::min(loads, 64 * issuers),
+                                       box_rows, k_boxes, row_tiles, private_regions, issuers, d,
+                                       err);
     cudaEventRecord(e0);
     cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, loads, box_rows, k_boxes,
-                                       row_tiles, d, err);
+                                       row_tiles, private_regions, issuers, d, err);
     cudaEventRecord(e1);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();

@@ -242,10 +242,16 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     const int unit = blockIdx.x / CG;
     const int num_units = gridDim.x / CG;
 
-    if (warp == 0 && lane == 0) {
+    if (warp == 0 && lane < 2) {
         // ------------------------------------------------------ TMA producer
-        // In a pair, both CTAs' loads complete on the leader's full barrier,
-        // which the leader arms with the bytes of both.
+        // Two issuing threads: a thread keeps only about one TMA box in
+        // progress at a time (measured: box rate per issuing thread is flat
+        // in ring depth and doubles with a second issuer), so lane 0 loads A
+        // and arms the stage barrier, lane 1 loads B. In a pair, both CTAs'
+        // loads complete on the leader's full barrier, which the leader arms
+        // with the bytes of both. A load may complete before its phase is
+        // armed; the phase cannot finish before lane 0 arrives.
+        const bool loads_a = lane == 0;
         const uint32_t leader_full0 = CG == 2 ? map_to_cta(full_bar(0), 0) : full_bar(0);
         int stage = 0;
         uint32_t phase = 0;
@@ -265,14 +271,20 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
                 const uint32_t sa = base + stage * T::kStageBytes;
                 if constexpr (CG == 1) {
-                    mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
-                    tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, a_row);
-                    tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK, b_row);
+                    if (loads_a) {
+                        mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
+                        tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, a_row);
+                    } else {
+                        tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK, b_row);
+                    }
                 } else {
-                    if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
                     const uint32_t fb = leader_full0 + 8u * stage;
-                    tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, a_row);
-                    tma_load_2d_pair(sa + T::kTileABytes, &tmap_b, fb, kb * BK, b_row);
+                    if (loads_a) {
+                        if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
+                        tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, a_row);
+                    } else {
+                        tma_load_2d_pair(sa + T::kTileABytes, &tmap_b, fb, kb * BK, b_row);
+                    }
                 }
                 ++issued;
                 if (++stage == stages) {
