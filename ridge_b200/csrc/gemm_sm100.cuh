@@ -242,20 +242,22 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     const int unit = blockIdx.x / CG;
     const int num_units = gridDim.x / CG;
 
-    if (warp == 0 && lane < 2) {
+    if (warp == 0 && lane < 4) {
         // ------------------------------------------------------ TMA producer
-        // Two issuing threads: a thread keeps only about one TMA box in
-        // progress at a time (measured: box rate per issuing thread is flat
-        // in ring depth and doubles with a second issuer), so lane 0 loads A
-        // and arms the stage barrier, lane 1 loads B. In a pair, both CTAs'
-        // loads complete on the leader's full barrier, which the leader arms
-        // with the bytes of both. A load may complete before its phase is
-        // armed; the phase cannot finish before lane 0 arrives.
-        const bool loads_a = lane == 0;
+        // Four issuing threads. One thread completes only about one TMA box
+        // every ~800 cycles whatever the box size or ring depth (measured by
+        // the calibration benchmark), so stages alternate between two lane
+        // pairs, and within a pair lane 2p loads A (and arms the stage
+        // barrier) while lane 2p+1 loads B. In a 2-CTA pair both CTAs' loads
+        // complete on the leader's full barrier, armed with the bytes of both.
+        // A load may complete before its phase is armed; the phase cannot
+        // finish before the arming lane arrives.
+        const bool loads_a = (lane & 1) == 0;
+        const int my_pair = lane >> 1;
         const uint32_t leader_full0 = CG == 2 ? map_to_cta(full_bar(0), 0) : full_bar(0);
         int stage = 0;
         uint32_t phase = 0;
-        long long issued = 0;
+        long long issued = 0;  // stages issued by all lanes so far (this lane's view)
         bool ok = true;
         WorkItem w;
         for (int it = 0; ok && get_item(p, unit, num_units, num_kb, it, w); ++it) {
@@ -264,26 +266,29 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             const int a_row = tm * BM + int(rank) * T::kRowsA;
             const int b_row = tn * BN + int(rank) * T::kRowsB;
             for (int kb = w.kb0; kb < w.kb1; ++kb) {
-                if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err,
-                               kErrTimeoutProducer)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t sa = base + stage * T::kStageBytes;
-                if constexpr (CG == 1) {
-                    if (loads_a) {
-                        mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
-                        tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, a_row);
-                    } else {
-                        tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK, b_row);
+                if (int(issued & 1) == my_pair) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err,
+                                   kErrTimeoutProducer)) {
+                        ok = false;
+                        break;
                     }
-                } else {
-                    const uint32_t fb = leader_full0 + 8u * stage;
-                    if (loads_a) {
-                        if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
-                        tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, a_row);
+                    const uint32_t sa = base + stage * T::kStageBytes;
+                    if constexpr (CG == 1) {
+                        if (loads_a) {
+                            mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
+                            tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, a_row);
+                        } else {
+                            tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK,
+                                        b_row);
+                        }
                     } else {
-                        tma_load_2d_pair(sa + T::kTileABytes, &tmap_b, fb, kb * BK, b_row);
+                        const uint32_t fb = leader_full0 + 8u * stage;
+                        if (loads_a) {
+                            if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
+                            tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, a_row);
+                        } else {
+                            tma_load_2d_pair(sa + T::kTileABytes, &tmap_b, fb, kb * BK, b_row);
+                        }
                     }
                 }
                 ++issued;
@@ -293,14 +298,16 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
             }
         }
-        if (!ok && leader) {
+        if (!ok && leader && loads_a) {
             // Abort path: let every load already in flight land before the CTA
             // can exit (in a pair the leader's barriers count the follower's
             // bytes too, and neither CTA exits before the final cluster
-            // barrier). Issue i went to stage i % stages with parity
-            // (i / stages) & 1; only the newest issue per stage can be pending.
+            // barrier). Stage issue i went to ring slot i % stages with parity
+            // (i / stages) & 1; only the newest issue per slot can be pending,
+            // and this lane armed the slots with i & 1 == my_pair.
             const long long first = issued > stages ? issued - stages : 0;
             for (long long i = first; i < issued; ++i) {
+                if (int(i & 1) != my_pair) continue;
                 mbar_wait(full_bar(int(i % stages)), uint32_t((i / stages) & 1), nullptr, p.err,
                           kErrTimeoutDrain);
             }
@@ -484,8 +491,10 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                         // lane, 64B-swizzled: 16-byte unit c of row r sits at
                         // unit c ^ ((r >> 1) & 3), conflict-free) and hand it to
                         // a TMA store, which clips rows/columns outside C.
+                        // Buffer b's stores are issued (and waited on) by lane b,
+                        // so the warp has two issuing threads.
                         const uint32_t sbuf = stage_buf0 + uint32_t(buf * T::kEpiChunkBytes);
-                        if (lane == 0) tma_store_wait_read<1>();  // buffer's previous store has read it
+                        if (lane == buf) tma_store_wait_read<0>();  // this buffer's last store has read it
                         __syncwarp();
                         const uint32_t row_addr = sbuf + uint32_t(lane * 64);
                         const uint32_t sw = uint32_t((lane >> 1) & 3);
@@ -499,7 +508,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                         }
                         fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) {
+                        if (lane == buf) {
                             tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0);
                             tma_store_commit();
                         }
@@ -545,7 +554,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 acc_phase ^= 1u;
             }
         }
-        if (p.tma_store && lane == 0) tma_store_wait_all<0>();
+        if (p.tma_store && lane < 2) tma_store_wait_all<0>();
     }
 
     tc_fence_before();
