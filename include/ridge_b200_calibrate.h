@@ -38,9 +38,15 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
                   int32_t private_regions, int32_t issuers, double* bytes_per_cycle_sm,
                   double* total_bytes_per_sec);
 
-/* Epilogue drain rate, bytes of FP16 C per SM cycle, for `warps` (4 or 8)
- * warps doing TMEM load -> convert -> swizzled smem -> TMA store. */
-int ridge_cal_epi(int32_t warps, double* bytes_per_cycle_sm);
+/* Epilogue drain rate, bytes of FP16 C per SM cycle (per SM) and per second
+ * (aggregate, optional), for `warps` (4 or 8) warps doing TMEM load -> convert
+ * -> swizzled smem -> TMA store into a C of c_bytes: L2-resident when small,
+ * HBM-bound when several times larger than L2. */
+int ridge_cal_epi(int32_t warps, int64_t c_bytes, double* bytes_per_cycle_sm,
+                  double* total_bytes_per_sec);
+
+/* Write-only bandwidth (cudaMemsetAsync over `bytes`), bytes per second. */
+int ridge_cal_write(int64_t bytes, double* bytes_per_sec);
 
 /* Device-to-device copy bandwidth over `bytes` (read + write bytes per second). */
 int ridge_cal_copy(int64_t bytes, double* bytes_per_sec);

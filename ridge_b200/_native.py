@@ -118,7 +118,8 @@ SIGNATURES = {
                                  C.POINTER(C.c_double)]),
     "ridge_cal_tma": (C.c_int, [_i64, _i32, _i32, _i32, _i32, _i32, C.POINTER(C.c_double),
                                 C.POINTER(C.c_double)]),
-    "ridge_cal_epi": (C.c_int, [_i32, C.POINTER(C.c_double)]),
+    "ridge_cal_epi": (C.c_int, [_i32, _i64, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "ridge_cal_write": (C.c_int, [_i64, C.POINTER(C.c_double)]),
     "ridge_cal_copy": (C.c_int, [_i64, C.POINTER(C.c_double)]),
     "ridge_cal_launch": (C.c_int, [C.POINTER(C.c_double)]),
     "ridge_cal_clock": (C.c_int, [C.POINTER(C.c_double)]),

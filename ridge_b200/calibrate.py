@@ -15,7 +15,9 @@ with the microbenchmarks built into libridge_b200.so
                      they add (cycles = sum); whichever fits the N sweep better
   l2BytesPerSec      aggregate TMA fill rate from an L2-resident tensor
   hbmBytesPerSec     aggregate TMA fill rate from a tensor 8x larger than L2
-  epiBytesPerCycleW4/W8  epilogue drain rate per SM with 4 / 8 warps
+  epiBytesPerCycleW4/W8  epilogue drain rate per SM with 4 / 8 warps (C in L2)
+  cWriteBytesPerSec  aggregate rate the epilogue writes a C far larger than L2
+  tmaBytesPerCycle   per-SM TMA fill with the GEMM's four issuing threads
   tmaLatencyCycles   load latency: bytes in flight / per-SM rate at depth 1
   launchOverheadSec  back-to-back launch cost of an empty kernel
   clockHz            SM clock measured under full tensor load
@@ -61,9 +63,15 @@ def tma(tensor_bytes, box_rows, depth, ctas=1, private=0, issuers=1):
     return per_sm.value, total.value
 
 
-def epi(warps):
+def epi(warps, c_bytes=32 << 20):
+    v, t = C.c_double(), C.c_double()
+    check(lib.ridge_cal_epi(warps, c_bytes, C.byref(v), C.byref(t)), "ridge_cal_epi")
+    return v.value, t.value
+
+
+def write_bw(nbytes=1 << 30):
     v = C.c_double()
-    check(lib.ridge_cal_epi(warps, C.byref(v)), "ridge_cal_epi")
+    check(lib.ridge_cal_write(nbytes, C.byref(v)), "ridge_cal_write")
     return v.value
 
 
@@ -166,10 +174,25 @@ def calibrate(verbose=True):
     raw["tma_l2_box128_depth_curve"] = curve
     res["tmaLatencyCycles"] = 128 * 128 / curve[1]
     log("tma latency (depth 1): %.0f cycles" % res["tmaLatencyCycles"])
-    res["epiBytesPerCycleW4"] = epi(4)
-    res["epiBytesPerCycleW8"] = epi(8)
-    log("epilogue: %.1f / %.1f B/cycle/SM (4 / 8 warps)" % (res["epiBytesPerCycleW4"],
-                                                           res["epiBytesPerCycleW8"]))
+    res["epiBytesPerCycleW4"], _ = epi(4)
+    res["epiBytesPerCycleW8"], _ = epi(8)
+    log("epilogue (C in L2): %.1f / %.1f B/cycle/SM (4 / 8 warps)" % (
+        res["epiBytesPerCycleW4"], res["epiBytesPerCycleW8"]))
+    big4, tot4 = epi(4, 1 << 30)
+    big8, tot8 = epi(8, 1 << 30)
+    raw["epi_hbm_w4"] = [big4, tot4]
+    raw["epi_hbm_w8"] = [big8, tot8]
+    res["cWriteBytesPerSec"] = max(tot4, tot8)
+    log("epilogue (C 1 GiB): %.1f / %.1f B/cycle/SM, %.2f / %.2f TB/s" % (
+        big4, big8, tot4 / 1e12, tot8 / 1e12))
+    raw["memset_bytes_per_sec"] = write_bw()
+    log("memset %.2f TB/s" % (raw["memset_bytes_per_sec"] / 1e12))
+    # the per-SM TMA fill with the GEMM's four issuing lanes; eight for headroom
+    per_sm4, tot4 = tma(32 << 20, 128, 2, 1, 0, 4)
+    per_sm8, tot8 = tma(32 << 20, 128, 1, 1, 0, 8)
+    res["tmaBytesPerCycle"] = per_sm4
+    raw["tma_l2_box128_d1_issuers8"] = [per_sm8, tot8]
+    log("tma fill, 4 issuers %.1f B/cycle/SM, 8 issuers %.1f" % (per_sm4, per_sm8))
     raw["copy_bytes_per_sec"] = copy_bw()
     res["launchOverheadSec"] = launch_overhead()
     log("copy %.2f TB/s, launch %.2f us" % (raw["copy_bytes_per_sec"] / 1e12,

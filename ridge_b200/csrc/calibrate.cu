@@ -55,9 +55,16 @@ __global__ void cal_umma_kernel(int m, int n, int iters, unsigned long long* cyc
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* p = smem_raw + (base - raw);
-    // A: 128 x 64 FP16 (16 KB); B: 256 x 64 FP16 (32 KB); zeros.
-    for (int i = threadIdx.x; i < (48 * 1024) / 16; i += blockDim.x)
-        reinterpret_cast<uint4*>(p)[i] = make_uint4(0, 0, 0, 0);
+    // A: 128 x 64 FP16 (16 KB); B: 256 x 64 FP16 (32 KB), filled with
+    // U(-1,1) values: tensor-core power, and with it the clock a power-capped
+    // part holds, depends on the data, so zeros would flatter the clock.
+    for (int i = threadIdx.x; i < (48 * 1024) / 2; i += blockDim.x) {
+        uint32_t h = uint32_t(i) * 2654435761u + blockIdx.x * 97u;
+        h ^= h >> 15;
+        h *= 2246822519u;
+        h ^= h >> 13;
+        reinterpret_cast<__half*>(p)[i] = __float2half(float(h & 0xffff) / 32768.0f - 1.0f);
+    }
     __shared__ uint64_t bar;
     __shared__ uint32_t tmem_slot;
     const int warp = threadIdx.x >> 5;
@@ -395,15 +402,17 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     return RIDGE_OK;
 }
 
-int ridge_cal_epi(int32_t warps, double* bytes_per_cycle_sm) {
-    if (!bytes_per_cycle_sm || !(warps == 4 || warps == 8)) return RIDGE_EINVAL;
+int ridge_cal_epi(int32_t warps, int64_t c_bytes, double* bytes_per_cycle_sm,
+                  double* total_bytes_per_sec) {
+    if (!bytes_per_cycle_sm || !(warps == 4 || warps == 8) || c_bytes < (8 << 20)) return RIDGE_EINVAL;
     auto enc = encoder();
     if (!enc) return RIDGE_ENOTSUP;
     int sms = 0;
     int st = sm_count(&sms);
     if (st) return st;
-    // C: 8192 x 2048 FP16 (32 MB), stored in 32 x 32 chunks.
-    const int64_t rows = 8192, cols = 2048;
+    // C: rows x 2048 FP16 (c_bytes), stored in 32 x 32 chunks, each chunk
+    // written once per pass.
+    const int64_t cols = 2048, rows = c_bytes / (cols * 2) / 32 * 32;
     void* c = nullptr;
     cudaError_t e = cudaMalloc(&c, size_t(rows * cols * 2));
     if (e != cudaSuccess) return int(e);
@@ -421,13 +430,18 @@ int ridge_cal_epi(int32_t warps, double* bytes_per_cycle_sm) {
     unsigned long long* d = nullptr;
     cudaMalloc(&d, sizeof(unsigned long long) * sms);
     cudaMemset(d, 0, sizeof(unsigned long long) * sms);
-    const int chunks = 2048;
-    const int smem = warps * 2 * 2048 + 1024;
     const int n_tiles = int((rows / 32) * (cols / 32));
+    const int chunks = int(std::max<int64_t>(64, int64_t(n_tiles) / (int64_t(sms) * warps)));
+    const int smem = warps * 2 * 2048 + 1024;
     cudaFuncSetAttribute(cal_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cal_epi_kernel<<<sms, warps * 32, smem>>>(map, 64, n_tiles, d);
     cudaMemset(d, 0, sizeof(unsigned long long) * sms);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0);
     cal_epi_kernel<<<sms, warps * 32, smem>>>(map, chunks, n_tiles, d);
+    cudaEventRecord(e1);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     std::vector<unsigned long long> h(sms);
@@ -436,6 +450,12 @@ int ridge_cal_epi(int32_t warps, double* bytes_per_cycle_sm) {
     cudaFree(c);
     if (e != cudaSuccess) return int(e);
     *bytes_per_cycle_sm = double(chunks) * warps * 2048 / median_cycles(h);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (total_bytes_per_sec)
+        *total_bytes_per_sec = double(chunks) * warps * 2048 * sms / (double(ms) * 1e-3);
     return RIDGE_OK;
 }
 
@@ -474,6 +494,33 @@ int ridge_cal_copy(int64_t bytes, double* bytes_per_sec) {
     cudaFree(b);
     if (e != cudaSuccess) return int(e);
     *bytes_per_sec = 2.0 * double(bytes) / (double(best) * 1e-3);
+    return RIDGE_OK;
+}
+
+int ridge_cal_write(int64_t bytes, double* bytes_per_sec) {
+    if (!bytes_per_sec || bytes < (1 << 24)) return RIDGE_EINVAL;
+    void* a = nullptr;
+    cudaError_t e = cudaMalloc(&a, size_t(bytes));
+    if (e != cudaSuccess) return int(e);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    float best = 1e30f;
+    for (int r = 0; r < 6; ++r) {
+        cudaEventRecord(e0);
+        cudaMemsetAsync(a, r, size_t(bytes));
+        cudaEventRecord(e1);
+        cudaEventSynchronize(e1);
+        float ms = 0;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (r > 0) best = std::min(best, ms);
+    }
+    e = cudaGetLastError();
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(a);
+    if (e != cudaSuccess) return int(e);
+    *bytes_per_sec = double(bytes) / (double(best) * 1e-3);
     return RIDGE_OK;
 }
 

@@ -522,11 +522,14 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                                 dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1],
                                                     packed[4 * v + 2], packed[4 * v + 3]);
                         } else {
-                            for (int e = 0; e < 32 && col0 + e < p.N; ++e) {
+                            // Ragged columns: element stores, fully unrolled so
+                            // `packed` stays in registers.
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
                                 const uint32_t word = packed[e >> 1];
                                 const unsigned short bits = (e & 1) ? (unsigned short)(word >> 16)
                                                                     : (unsigned short)(word & 0xffff);
-                                crow[col0 + e] = __ushort_as_half(bits);
+                                if (col0 + e < p.N) crow[col0 + e] = __ushort_as_half(bits);
                             }
                         }
                     }
