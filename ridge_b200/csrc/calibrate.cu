@@ -180,7 +180,7 @@ __global__ void cal_epi_kernel(const __grid_constant__ CUtensorMap cmap, int chu
     for (int c = 0; c < chunks; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + (uint32_t(quad * 32) << 16) + uint32_t((c % 8) * 32), r);
-        tmem_wait_ld();
+        tmem_wait_ld(r);
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {

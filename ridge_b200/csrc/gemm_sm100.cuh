@@ -425,8 +425,25 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
             }
             __syncwarp();
-#pragma unroll
-            for (int h = 0; h < T::kMHalves; ++h) {
+            // This warp's chunks of the tile, in order: M-half h, column chunk
+            // j = group, group + kGroups, ... The TMEM load of chunk ci + 1 is
+            // issued before chunk ci is stored, so its latency hides behind
+            // the stores.
+            constexpr int kPerHalf = kChunks / kGroups;
+            constexpr int kPerWarp = T::kMHalves * kPerHalf;
+            auto chunk_taddr = [&](int ci) {
+                const int hh = ci / kPerHalf, jj = group + (ci % kPerHalf) * kGroups;
+                return tmem_base + (uint32_t(quad * 32) << 16) +
+                       uint32_t(acc * T::kAccCols + hh * BN + jj * 32);
+            };
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(chunk_taddr(0), r);
+            tmem_wait_ld(r);
+#pragma unroll 1
+            for (int ci = 0; ci < kPerWarp; ++ci) {
+                const int h = ci / kPerHalf;
+                const int j = group + (ci % kPerHalf) * kGroups;
+                const bool more = ci + 1 < kPerWarp;
                 // M=128 / 256-pair UMMA: row r of this CTA lives in TMEM lane r.
                 // M=64 UMMA: rows 16q..16q+15 live in lanes 32q..32q+15.
                 const int warp_row0 = BM == 64 ? quad * 16 : h * 128 + quad * 32;
@@ -436,14 +453,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 const bool row_ok = row_live && row < p.M;
                 // A warp whose rows all lie at or beyond M has nothing to reduce.
                 const bool warp_live = (long long)tile_row0 + warp_row0 < p.M;
-#pragma unroll 1
-                for (int j = group; j < kChunks; j += kGroups) {
-                    uint32_t r[32];
-                    const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) +
-                                           uint32_t(acc * T::kAccCols + h * BN + j * 32);
-                    __syncwarp();
-                    tmem_ld_32x32b_x32(taddr, r);
-                    tmem_wait_ld();
+                {
                     // Split-K partial chunks use a lane-contiguous layout: float4
                     // v of lane L of chunk c sits at ((c * 8 + v) * 32 + L), so
                     // every warp-wide store or load covers 512 contiguous bytes.
@@ -461,6 +471,11 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                                                                  __uint_as_float(r[4 * v + 1]),
                                                                  __uint_as_float(r[4 * v + 2]),
                                                                  __uint_as_float(r[4 * v + 3])));
+                        }
+                        if (more) {
+                            __syncwarp();
+                            tmem_ld_32x32b_x32(chunk_taddr(ci + 1), r);
+                            tmem_wait_ld(r);
                         }
                         continue;  // warp-uniform: w.split is the same on every lane
                     }
@@ -485,6 +500,10 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                    if (more) {
+                        __syncwarp();
+                        tmem_ld_32x32b_x32(chunk_taddr(ci + 1), r);  // lands while we store
+                    }
                     const int col0 = tn * BN + j * 32;
                     if (p.tma_store) {
                         // Stage this warp's 32 x 32 chunk (one 64-byte row per
@@ -533,6 +552,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                             }
                         }
                     }
+                    if (more) tmem_wait_ld(r);
                 }
             }
             if (w.split > 0) {
