@@ -196,13 +196,16 @@ int ridge_fill_lcg(void* out_f16, int64_t n, uint32_t* state, int32_t range, voi
 typedef struct ridge_hw {
     char name[64];
     int32_t num_sms;
-    double clock_hz;                 /* SM clock under load */
+    double clock_hz;                 /* [CAL] SM clock under sustained tensor load (power cap) */
     double umma_cycles_128x256;      /* [CAL] SM cycles per 128x256x16 FP16 tcgen05.mma */
     double umma_m64_ratio;           /* [CAL] cycles of a 64xNx16 MMA / cycles of 128xNx16 */
     double smem_bytes_per_cycle;     /* [CAL] operand bytes/cycle/SM the tensor core reads */
     double smem_mma_overlap;         /* [CAL] 1: operand reads overlap the MMA (max); 0: in series (sum) */
     double l2_bytes_per_sec;         /* [CAL] aggregate TMA L2 -> SM fill bandwidth */
-    double hbm_bytes_per_sec;        /* [CAL] whole-GPU HBM bandwidth */
+    double hbm_bytes_per_sec;        /* [CAL] whole-GPU HBM read bandwidth (TMA streaming) */
+    double tma_box_cycles;           /* [CAL] cycles per TMA box per issuing thread, 4 threads issuing */
+    double pipeline_efficiency;      /* [CAL] steady-state mainloop rate / ideal, from a calibration GEMM */
+    double c_write_bytes_per_sec;    /* [CAL] epilogue write rate of a C far larger than L2 */
     double epi_bytes_per_cycle_w4;   /* [CAL] C bytes/cycle/SM drained by 4 epilogue warps */
     double epi_bytes_per_cycle_w8;   /* [CAL] same with 8 epilogue warps */
     double tma_latency_cycles;       /* [CAL] issue -> arrival latency of one stage load */

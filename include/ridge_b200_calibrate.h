@@ -41,9 +41,11 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
 /* Epilogue drain rate, bytes of FP16 C per SM cycle (per SM) and per second
  * (aggregate, optional), for `warps` (4 or 8) warps doing TMEM load -> convert
  * -> swizzled smem -> TMA store into a C of c_bytes: L2-resident when small,
- * HBM-bound when several times larger than L2. */
-int ridge_cal_epi(int32_t warps, int64_t c_bytes, double* bytes_per_cycle_sm,
-                  double* total_bytes_per_sec);
+ * HBM-bound when several times larger than L2. tile_pattern 0: each warp
+ * writes consecutive 32 x 32 chunks along rows; 1: the GEMM's order (each CTA
+ * writes whole 128 x 256 tiles, a warp its 32-row quarter). */
+int ridge_cal_epi(int32_t warps, int64_t c_bytes, int32_t tile_pattern,
+                  double* bytes_per_cycle_sm, double* total_bytes_per_sec);
 
 /* Write-only bandwidth (cudaMemsetAsync over `bytes`), bytes per second. */
 int ridge_cal_write(int64_t bytes, double* bytes_per_sec);

@@ -43,6 +43,8 @@ class HwC(C.Structure):
                 ("umma_cycles_128x256", C.c_double), ("umma_m64_ratio", C.c_double),
                 ("smem_bytes_per_cycle", C.c_double), ("smem_mma_overlap", C.c_double),
                 ("l2_bytes_per_sec", C.c_double), ("hbm_bytes_per_sec", C.c_double),
+                ("tma_box_cycles", C.c_double), ("pipeline_efficiency", C.c_double),
+                ("c_write_bytes_per_sec", C.c_double),
                 ("epi_bytes_per_cycle_w4", C.c_double), ("epi_bytes_per_cycle_w8", C.c_double),
                 ("tma_latency_cycles", C.c_double), ("launch_overhead_sec", C.c_double),
                 ("l2_bytes", C.c_double), ("smem_bytes_per_sm", C.c_int32),
@@ -118,7 +120,8 @@ SIGNATURES = {
                                  C.POINTER(C.c_double)]),
     "ridge_cal_tma": (C.c_int, [_i64, _i32, _i32, _i32, _i32, _i32, C.POINTER(C.c_double),
                                 C.POINTER(C.c_double)]),
-    "ridge_cal_epi": (C.c_int, [_i32, _i64, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "ridge_cal_epi": (C.c_int, [_i32, _i64, _i32, C.POINTER(C.c_double),
+                                C.POINTER(C.c_double)]),
     "ridge_cal_write": (C.c_int, [_i64, C.POINTER(C.c_double)]),
     "ridge_cal_copy": (C.c_int, [_i64, C.POINTER(C.c_double)]),
     "ridge_cal_launch": (C.c_int, [C.POINTER(C.c_double)]),

@@ -63,9 +63,10 @@ def tma(tensor_bytes, box_rows, depth, ctas=1, private=0, issuers=1):
     return per_sm.value, total.value
 
 
-def epi(warps, c_bytes=32 << 20):
+def epi(warps, c_bytes=32 << 20, tile_pattern=0):
     v, t = C.c_double(), C.c_double()
-    check(lib.ridge_cal_epi(warps, c_bytes, C.byref(v), C.byref(t)), "ridge_cal_epi")
+    check(lib.ridge_cal_epi(warps, c_bytes, tile_pattern, C.byref(v), C.byref(t)),
+          "ridge_cal_epi")
     return v.value, t.value
 
 
@@ -85,6 +86,43 @@ def launch_overhead():
     v = C.c_double()
     check(lib.ridge_cal_launch(C.byref(v)), "ridge_cal_launch")
     return v.value
+
+
+# The one constant taken from the GEMM itself: a long, tensor-bound launch on a
+# shape outside the validation sweep, with every other constant already
+# measured; efficiency = measured / modelled-at-efficiency-1.
+def _cal_gemm():
+    from .gemm import TileConfig
+    return (6144, 6144, 6144, TileConfig(256, 256, 64, 5, 4, 8, 2))
+
+
+CAL_GEMM = None
+
+
+def pipeline_efficiency(res):
+    global CAL_GEMM
+    import torch
+
+    from ._native import HwC
+    from .gemm import synthetic_inputs
+    from .model import HW_KEYS, predict
+    CAL_GEMM = _cal_gemm()
+    M, N, K, cfg = CAL_GEMM
+    a, b = synthetic_inputs(M, N, K)
+    c = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    ms = C.c_double()
+    cc = cfg.to_c()
+    check(lib.ridge_time_gemm(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, K,
+                              K, N, 10, 50, torch.cuda.current_stream().cuda_stream,
+                              C.byref(ms)), "ridge_time_gemm")
+    meas = 2.0 * M * N * K / (ms.value * 1e-3) / 1e12
+    hw = HwC()
+    lib.ridge_hw_b200(C.byref(hw))
+    for k, f in HW_KEYS.items():
+        if k in res:
+            setattr(hw, f, type(getattr(hw, f))(res[k]))
+    ideal = predict(M, N, K, cfg, hw)["predicted_tflops"]
+    return min(1.0, meas / ideal), meas, ideal
 
 
 def fit_smem(cycles_by_n, m=128):
@@ -182,9 +220,15 @@ def calibrate(verbose=True):
     big8, tot8 = epi(8, 1 << 30)
     raw["epi_hbm_w4"] = [big4, tot4]
     raw["epi_hbm_w8"] = [big8, tot8]
-    res["cWriteBytesPerSec"] = max(tot4, tot8)
-    log("epilogue (C 1 GiB): %.1f / %.1f B/cycle/SM, %.2f / %.2f TB/s" % (
+    log("epilogue (C 1 GiB, row stripes): %.1f / %.1f B/cycle/SM, %.2f / %.2f TB/s" % (
         big4, big8, tot4 / 1e12, tot8 / 1e12))
+    t4, tt4 = epi(4, 1 << 30, 1)
+    t8, tt8 = epi(8, 1 << 30, 1)
+    raw["epi_hbm_tiles_w4"] = [t4, tt4]
+    raw["epi_hbm_tiles_w8"] = [t8, tt8]
+    res["cWriteBytesPerSec"] = max(tt4, tt8)
+    log("epilogue (C 1 GiB, GEMM tile order): %.1f / %.1f B/cycle/SM, %.2f / %.2f TB/s" % (
+        t4, t8, tt4 / 1e12, tt8 / 1e12))
     raw["memset_bytes_per_sec"] = write_bw()
     log("memset %.2f TB/s" % (raw["memset_bytes_per_sec"] / 1e12))
     # the per-SM TMA fill with the GEMM's four issuing lanes; eight for headroom
@@ -199,6 +243,14 @@ def calibrate(verbose=True):
                                            res["launchOverheadSec"] * 1e6))
     res.update({"numSMs": 148, "l2Bytes": 126.0 * 1024 * 1024, "smemBytesPerSM": 233472,
                 "tmemColsPerSM": 512, "maxCtasPerSM": 32})
+    res["tmaBoxCycles"] = 4 * 128 * 128 / res.pop("tmaBytesPerCycle")
+    res["pipelineEfficiency"] = 1.0
+    eff, meas, ideal = pipeline_efficiency(res)
+    res["pipelineEfficiency"] = eff
+    raw["calibration_gemm"] = {"shape": list(CAL_GEMM[:3]), "config": CAL_GEMM[3].tag(),
+                               "measured_tflops": meas, "model_tflops_at_efficiency_1": ideal}
+    log("calibration GEMM %s %s: %.1f TF measured, %.1f ideal -> pipeline efficiency %.3f" % (
+        "x".join(map(str, CAL_GEMM[:3])), CAL_GEMM[3].tag(), meas, ideal, eff))
     bad = {k: v for k, v in res.items() if k in BANDS and not BANDS[k][0] <= v <= BANDS[k][1]}
     return res, raw, bad
 

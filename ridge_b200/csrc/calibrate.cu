@@ -159,7 +159,7 @@ __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int dept
 // them 64B-swizzled in shared memory and TMA-store them to C, the same
 // sequence as the GEMM epilogue; `chunks` chunks per warp.
 __global__ void cal_epi_kernel(const __grid_constant__ CUtensorMap cmap, int chunks, int n_tiles,
-                               unsigned long long* cycles) {
+                               int tile_pattern, unsigned long long* cycles) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -199,8 +199,26 @@ __global__ void cal_epi_kernel(const __grid_constant__ CUtensorMap cmap, int chu
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            const int t = (int(blockIdx.x) * 64 + warp * chunks + c) % n_tiles;
-            tma_store_2d(&cmap, sb, (t % 64) * 32, (t / 64) * 32);
+            int x, y;
+            if (tile_pattern) {
+                // GEMM order: CTA b writes whole 128 x 256 tiles b, b + grid,
+                // ...; warp w owns rows 32*(w%4) and every (warps/4)-th of the
+                // eight 32-column chunks of each row block.
+                const int groups = blockDim.x / 128;
+                const int per_tile = 8 / groups;
+                const int tile = int(blockIdx.x) + (c / per_tile) * int(gridDim.x);
+                const int tiles_per_row = 2048 / 256;
+                const int tr = (tile / tiles_per_row) % (n_tiles / 256);
+                const int tc = tile % tiles_per_row;
+                const int chunk = (warp / 4) + (c % per_tile) * groups;
+                x = tc * 256 + chunk * 32;
+                y = tr * 128 + (warp & 3) * 32;
+            } else {
+                const int t = (int(blockIdx.x) * 64 + warp * chunks + c) % n_tiles;
+                x = (t % 64) * 32;
+                y = (t / 64) * 32;
+            }
+            tma_store_2d(&cmap, sb, x, y);
             tma_store_commit();
         }
         buf ^= 1;
@@ -402,8 +420,8 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     return RIDGE_OK;
 }
 
-int ridge_cal_epi(int32_t warps, int64_t c_bytes, double* bytes_per_cycle_sm,
-                  double* total_bytes_per_sec) {
+int ridge_cal_epi(int32_t warps, int64_t c_bytes, int32_t tile_pattern,
+                  double* bytes_per_cycle_sm, double* total_bytes_per_sec) {
     if (!bytes_per_cycle_sm || !(warps == 4 || warps == 8) || c_bytes < (8 << 20)) return RIDGE_EINVAL;
     auto enc = encoder();
     if (!enc) return RIDGE_ENOTSUP;
@@ -434,13 +452,13 @@ int ridge_cal_epi(int32_t warps, int64_t c_bytes, double* bytes_per_cycle_sm,
     const int chunks = int(std::max<int64_t>(64, int64_t(n_tiles) / (int64_t(sms) * warps)));
     const int smem = warps * 2 * 2048 + 1024;
     cudaFuncSetAttribute(cal_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cal_epi_kernel<<<sms, warps * 32, smem>>>(map, 64, n_tiles, d);
+    cal_epi_kernel<<<sms, warps * 32, smem>>>(map, 64, n_tiles, tile_pattern, d);
     cudaMemset(d, 0, sizeof(unsigned long long) * sms);
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventRecord(e0);
-    cal_epi_kernel<<<sms, warps * 32, smem>>>(map, chunks, n_tiles, d);
+    cal_epi_kernel<<<sms, warps * 32, smem>>>(map, chunks, n_tiles, tile_pattern, d);
     cudaEventRecord(e1);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();

@@ -127,21 +127,24 @@ extern "C" {
 
 // Datasheet-derived placeholders (replaced by a calibration file):
 //   148 SMs; 8192 dense FP16 FLOP/cycle/SM, so one 128x256x16 MMA
-//   (1,048,576 FLOP) takes 128 cycles; 2.25 PFLOP/s needs ~1.86 GHz;
-//   shared memory feeds 128 B/cycle/SM; HBM3e 8 TB/s nominal, 6.5 TB/s
-//   copy-measured on this pool; L2 126 MB.
+//   (1,048,576 FLOP) takes 128 cycles; 2.25 PFLOP/s needs ~1.86 GHz, but a
+//   1 kW part holds about 1.4 GHz under sustained tensor load; shared memory
+//   feeds 128 B/cycle/SM; HBM3e 8 TB/s nominal; L2 126 MB.
 int ridge_hw_b200(ridge_hw* h) {
     if (!h) return RIDGE_EINVAL;
     std::memset(h, 0, sizeof(*h));
     std::snprintf(h->name, sizeof(h->name), "B200 (datasheet placeholders)");
     h->num_sms = 148;
-    h->clock_hz = 1.86e9;
+    h->clock_hz = 1.4e9;
     h->umma_cycles_128x256 = 128.0;
     h->umma_m64_ratio = 1.0;
     h->smem_bytes_per_cycle = 128.0;
     h->smem_mma_overlap = 1.0;
     h->l2_bytes_per_sec = 20e12;
     h->hbm_bytes_per_sec = 6.5e12;
+    h->tma_box_cycles = 1030.0;
+    h->pipeline_efficiency = 0.9;
+    h->c_write_bytes_per_sec = 6.5e12;
     h->epi_bytes_per_cycle_w4 = 32.0;
     h->epi_bytes_per_cycle_w8 = 48.0;
     h->tma_latency_cycles = 1000.0;
@@ -187,6 +190,9 @@ int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t er
                {"smemMmaOverlap", &h.smem_mma_overlap},
                {"l2BytesPerSec", &h.l2_bytes_per_sec},
                {"hbmBytesPerSec", &h.hbm_bytes_per_sec},
+               {"tmaBoxCycles", &h.tma_box_cycles},
+               {"pipelineEfficiency", &h.pipeline_efficiency},
+               {"cWriteBytesPerSec", &h.c_write_bytes_per_sec},
                {"epiBytesPerCycleW4", &h.epi_bytes_per_cycle_w4},
                {"epiBytesPerCycleW8", &h.epi_bytes_per_cycle_w8},
                {"tmaLatencyCycles", &h.tma_latency_cycles},
@@ -217,7 +223,8 @@ int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t er
     // ceiling are refused rather than loaded.
     if (h.num_sms <= 0 || h.clock_hz <= 0 || h.umma_cycles_128x256 <= 0 ||
         h.umma_m64_ratio <= 0 || h.smem_bytes_per_cycle <= 0 || h.l2_bytes_per_sec <= 0 ||
-        h.hbm_bytes_per_sec <= 0 || h.epi_bytes_per_cycle_w4 <= 0 ||
+        h.hbm_bytes_per_sec <= 0 || h.tma_box_cycles <= 0 || h.pipeline_efficiency <= 0 || h.pipeline_efficiency > 1 || h.c_write_bytes_per_sec <= 0 ||
+        h.epi_bytes_per_cycle_w4 <= 0 ||
         h.epi_bytes_per_cycle_w8 <= 0 || h.tma_latency_cycles < 0 || h.launch_overhead_sec < 0 ||
         h.l2_bytes <= 0 || h.smem_bytes_per_sm <= 0 || h.tmem_cols_per_sm <= 0 ||
         h.max_ctas_per_sm <= 0 || h.smem_mma_overlap < 0 || h.smem_mma_overlap > 1) {

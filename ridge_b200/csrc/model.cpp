@@ -149,59 +149,94 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     p.ctas_per_sm = cps;
     p.acc_buffers = info.acc_buffers;
 
-    // ---- one K-block (BK) of one CTA, in SM cycles
+    // ---- one pipeline stage (BK of K) of one CTA, in SM cycles at the
+    // clock the part holds under sustained tensor load.
     const double kb = std::ceil(double(K) / t.BK);
-    const double mma_per_kb = double(g.halves) * (t.BK / 16);
-    const double t_mma_one = hw->umma_cycles_128x256 * (double(t.BN) / 256.0) * g.mma_m_ratio;
-    const double t_mma = mma_per_kb * t_mma_one;
-    // Operand bytes the tensor core reads per K-block on this SM: the A rows
-    // this CTA holds, and B once per M-half (a 2-CTA pair splits B's columns).
-    const double smem_read =
-        double(g.rows_per_cta) * t.BK * 2.0 + double(g.halves) * (double(t.BN) / g.cg) * t.BK * 2.0;
-    const double t_smem = smem_read / hw->smem_bytes_per_cycle;
+    const double mma_per_stage = double(g.halves) * (t.BK / 16);
+    // One tcgen05.mma on this SM: N/256 of a 128x256x16 MMA, unless reading
+    // its operands from shared memory takes longer (A: the 128 -- or 64 --
+    // rows this SM multiplies; B: the BN columns it holds, half of them in a
+    // 2-CTA pair, whose peer reads the other half).
+    const double a_rows = t.BM == 64 ? 64.0 : 128.0;
+    const double b_cols = double(t.BN) / g.cg;
+    const double t_issue = hw->umma_cycles_128x256 * (double(t.BN) / 256.0) * g.mma_m_ratio;
+    const double t_read = (a_rows + b_cols) * 16.0 * 2.0 / hw->smem_bytes_per_cycle;
     const double ov = std::min(1.0, std::max(0.0, hw->smem_mma_overlap));
-    const double t_step = ov * std::max(t_mma, t_smem) + (1.0 - ov) * (t_mma + t_smem);
-    // TMA fill from L2, with every SM loading at once.
-    const double tma_bytes = (double(g.rows_per_cta) + double(t.BN) / g.cg) * t.BK * 2.0;
-    const double l2_bpc_sm = hw->l2_bytes_per_sec / (hw->clock_hz * hw->num_sms);
-    const double t_l2 = tma_bytes / l2_bpc_sm;
+    const double t_one = ov * std::max(t_issue, t_read) + (1.0 - ov) * (t_issue + t_read);
+    const double t_mma = mma_per_stage * t_one;
+    // TMA fill: a stage is one box of A and one of B, each issued by its own
+    // thread, and stages alternate between two such thread pairs. An issuing
+    // thread finishes about one box per tma_box_cycles whatever the box size
+    // (measured), so a CTA fills one stage per tma_box_cycles / 2.
+    const double t_fill = hw->tma_box_cycles / 2.0;
+    const double stage_bytes = (double(g.rows_per_cta) + double(t.BN) / g.cg) * t.BK * 2.0;
+    (void)stage_bytes;
+    const double t_smem = mma_per_stage * t_read;
 
-    // ---- residency and the persistent walk
+    // ---- residency and the persistent walk (with the launcher's split-K tail)
     const int64_t num_m = (M + t.BM - 1) / t.BM;
     const int64_t num_n = (N + t.BN - 1) / t.BN;
     const int64_t tiles = num_m * num_n;
-    const int64_t units_per_sm_round = int64_t(hw->num_sms / g.cg) * cps;
-    const int64_t slots = std::max<int64_t>(1, units_per_sm_round);
-    const int64_t grid_units = std::min(tiles, slots);
-    const double tiles_per_unit = std::ceil(double(tiles) / double(grid_units));
+    const int64_t units = std::max<int64_t>(1, int64_t(hw->num_sms / g.cg) * cps);
+    const int64_t rem = tiles >= units ? tiles % units : tiles;
+    int64_t splits = 1;
+    if (t.split_k != 1 && rem > 0)
+        splits = std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(units / rem, 8),
+                                                        int64_t(kb)));
+    const int64_t dp_tiles = splits >= 2 ? tiles - rem : tiles;
+    const int64_t grid_units = std::max(std::min(tiles, units), splits >= 2 ? rem * splits : 0);
     // CTAs actually sharing one SM (a small grid leaves SMs with fewer).
-    const double resident = std::max(1.0, double(grid_units) * g.cg / hw->num_sms);
+    const double resident =
+        std::min(double(cps), std::max(1.0, double(grid_units) * g.cg / hw->num_sms));
 
-    // Shared on-SM resources (tensor core, smem port) are divided among the
-    // resident CTAs; the latency each CTA must hide is not.
-    const double t_kblock = std::max(t_step, t_l2) * resident;
-    const double t_period = std::max(t_kblock, (hw->tma_latency_cycles + t_kblock) / t.stages);
-    const double t_main = kb * t_period;
+    // Shared on-SM resources (tensor core, shared memory) serve the resident
+    // CTAs in turn; each CTA's fill and its load latency are its own.
+    // The SM keeps about four boxes in flight in all (one CTA with four
+    // issuing threads already reaches it), so resident CTAs share that
+    // budget exactly like they share the tensor core.
+    const double t_stage = std::max(t_mma, t_fill) * resident / hw->pipeline_efficiency;
+    // A ring slot refills only after its MMAs finish: the load then waits
+    // behind the pair's current box (t_fill) and travels for the unloaded
+    // latency, so `stages` slots must cover (latency + t_fill + t_stage).
+    const double t_period = std::max(
+        t_stage, (hw->tma_latency_cycles + t_fill + t_stage) / double(t.stages));
+    const double t_main_whole = kb * t_period;
 
     const double c_bytes_tile = double(g.rows_per_cta) * t.BN * 2.0;
     const double epi_bpc = t.warps == 8 ? hw->epi_bytes_per_cycle_w8 : hw->epi_bytes_per_cycle_w4;
-    const double t_epi = c_bytes_tile / epi_bpc * resident;
-    double t_unit;
-    double t_tile;
-    if (info.acc_buffers >= 2) {
-        t_tile = std::max(t_main, t_epi);
-        t_unit = tiles_per_unit * t_tile + std::min(t_main, t_epi);
-    } else {
-        t_tile = t_main + t_epi;
-        t_unit = tiles_per_unit * t_tile;
+    const double t_epi = c_bytes_tile / epi_bpc;
+    auto tile_period = [&](double t_main) {
+        return info.acc_buffers >= 2 ? std::max(t_main, t_epi) : t_main + t_epi;
+    };
+    const double dp_rounds = std::ceil(double(dp_tiles) / double(std::min(units, std::max<int64_t>(dp_tiles, 1))));
+    const double dp_per_unit = dp_tiles > 0 ? std::ceil(double(dp_tiles) / double(std::min(tiles, units))) : 0.0;
+    (void)dp_rounds;
+    double t_unit = dp_per_unit * tile_period(t_main_whole);
+    double t_sk = 0.0;
+    if (splits >= 2) {
+        // One K range of 1/splits, then the owner folds in splits - 1 FP32
+        // partial tiles (read at the fill rate) before its epilogue.
+        const double partial_bytes = double(g.rows_per_cta) * t.BN * 4.0;
+        t_sk = std::ceil(kb / double(splits)) * t_period +
+               double(splits - 1) * partial_bytes / (2.0 * epi_bpc) + t_epi;
+        t_unit += t_sk;
+    } else if (info.acc_buffers >= 2 && dp_per_unit > 0) {
+        t_unit += std::min(t_main_whole, t_epi);  // the last tile's epilogue drains alone
     }
     const double t_prologue = hw->tma_latency_cycles;
     t_unit += t_prologue;
     const double compute_sec = t_unit / hw->clock_hz + hw->launch_overhead_sec;
 
-    // ---- HBM
-    const double dram = dram_bytes(M, N, K, t.BM, t.BN, t.groupM, grid_units, hw->l2_bytes);
-    const double hbm_sec = dram / hw->hbm_bytes_per_sec + hw->launch_overhead_sec;
+    // ---- HBM: operand reads (grouped-M walk, L2 reuse), C writes, split-K partials
+    const double a_b_reads =
+        dram_bytes(M, N, K, t.BM, t.BN, t.groupM, std::min(tiles, units), hw->l2_bytes) -
+        double(M) * N * 2.0;
+    const double c_write = double(M) * N * 2.0;
+    const double partial_traffic =
+        splits >= 2 ? 2.0 * double(rem) * (splits - 1) * g.cg * double(g.rows_per_cta) * t.BN * 4.0
+                    : 0.0;
+    const double hbm_sec = a_b_reads / hw->hbm_bytes_per_sec + c_write / hw->c_write_bytes_per_sec +
+                           partial_traffic / hw->c_write_bytes_per_sec + hw->launch_overhead_sec;
 
     const double flops = 2.0 * double(M) * double(N) * double(K);
     const double peak_flops_per_cycle_sm = 2.0 * 128.0 * 256.0 * 16.0 / hw->umma_cycles_128x256;
@@ -210,31 +245,33 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     p.hbm_tflops = flops / hbm_sec / 1e12;
     p.predicted_seconds = std::max(compute_sec, hbm_sec);
     p.predicted_tflops = flops / p.predicted_seconds / 1e12;
-    p.dram_bytes = dram;
-    p.arithmetic_intensity = flops / dram;
+    p.dram_bytes = a_b_reads + c_write;
+    p.arithmetic_intensity = flops / p.dram_bytes;
 
     p.k_blocks = kb;
     p.t_mma_cycles = t_mma;
     p.t_smem_cycles = t_smem;
-    p.t_l2_cycles = t_l2;
-    p.t_step_cycles = t_step;
+    p.t_l2_cycles = t_fill;
+    p.t_step_cycles = t_stage;
     p.t_period_cycles = t_period;
     p.t_epilogue_cycles = t_epi;
-    p.t_tile_cycles = t_tile;
+    p.t_tile_cycles = tile_period(t_main_whole);
     p.t_prologue_cycles = t_prologue;
     p.total_tiles = double(tiles);
-    p.tile_slots = double(slots);
-    p.waves_exact = double(tiles) / double(slots);
+    p.tile_slots = double(units);
+    p.waves_exact = double(tiles) / double(units);
 
-    p.smem_efficiency = t_mma / t_step;
-    p.l2_efficiency = t_step / std::max(t_step, t_l2);
-    p.occ_factor = t_kblock / t_period;
-    // Busy share of the machine's tile slots over the kernel: a partial last
-    // round, or a grid smaller than one round, leaves slots idle.
-    p.wave_efficiency = double(tiles) / (tiles_per_unit * double(slots));
-    p.epilogue_efficiency = t_main / t_tile;
-    const double body = tiles_per_unit * t_tile;
-    p.envelope_efficiency = body / (t_unit + hw->launch_overhead_sec * hw->clock_hz);
+    // Efficiency factors (1 = not limiting); the worst one names the label.
+    const double ideal_unit = double(tiles) * kb * (mma_per_stage * t_issue) / double(units);
+    p.smem_efficiency = t_issue / t_one;
+    p.l2_efficiency = std::min(1.0, t_mma * resident / t_stage);
+    p.occ_factor = t_stage / t_period;
+    p.wave_efficiency = double(tiles) * kb * t_period / (double(units) * (t_unit - t_prologue));
+    p.wave_efficiency = std::min(1.0, p.wave_efficiency);
+    p.epilogue_efficiency = t_main_whole / tile_period(t_main_whole);
+    p.envelope_efficiency =
+        std::min(1.0, (t_unit - t_prologue) / (t_unit + hw->launch_overhead_sec * hw->clock_hz));
+    (void)ideal_unit;
 
     if (hbm_sec > compute_sec) {
         p.bottleneck = RIDGE_BOTTLENECK_HBM;

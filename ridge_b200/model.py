@@ -22,7 +22,9 @@ HW_KEYS = {  # JSON key -> struct field
     "numSMs": "num_sms", "clockHz": "clock_hz", "ummaCycles128x256": "umma_cycles_128x256",
     "ummaM64Ratio": "umma_m64_ratio", "smemBytesPerCycle": "smem_bytes_per_cycle",
     "smemMmaOverlap": "smem_mma_overlap", "l2BytesPerSec": "l2_bytes_per_sec",
-    "hbmBytesPerSec": "hbm_bytes_per_sec", "epiBytesPerCycleW4": "epi_bytes_per_cycle_w4",
+    "hbmBytesPerSec": "hbm_bytes_per_sec", "tmaBoxCycles": "tma_box_cycles",
+    "pipelineEfficiency": "pipeline_efficiency",
+    "cWriteBytesPerSec": "c_write_bytes_per_sec", "epiBytesPerCycleW4": "epi_bytes_per_cycle_w4",
     "epiBytesPerCycleW8": "epi_bytes_per_cycle_w8", "tmaLatencyCycles": "tma_latency_cycles",
     "launchOverheadSec": "launch_overhead_sec", "l2Bytes": "l2_bytes",
     "smemBytesPerSM": "smem_bytes_per_sm", "tmemColsPerSM": "tmem_cols_per_sm",
