@@ -35,7 +35,8 @@ constexpr int kMaxDynSmem = 232448;   // 227 KB opt-in limit per CTA on sm_100
 constexpr int kSmemPerSm = 233472;    // 228 KB per SM
 constexpr int kSmemReservedPerCta = 1024;
 constexpr int kTmemColsPerSm = 512;
-constexpr int64_t kCounterBytes = 64 * 1024;  // split-K counter area at the head of a workspace
+constexpr int64_t kCounterBytes = 64 * 1024;
+constexpr int64_t kMinSplitBlocks = 4;  // K-blocks per split-K range, at least  // split-K counter area at the head of a workspace
 
 const std::vector<KernelEntry>& registry() {
     static const std::vector<KernelEntry> entries = [] {
@@ -288,7 +289,7 @@ int ensure_smem_attr(const KernelEntry& e, int idx, DeviceState* dev) {
 // Grid size and split-K tail for one launch. With U resident units and T
 // tiles, whole tiles fill floor(T / U) rounds; the R = T mod U tiles of a
 // partial last round (all T when T < U) are split along K into
-// s = floor(U / R) ranges (at most 8, at most the K-block count) so the round
+// s = floor(U / R) ranges (at most 8, at least 4 K-blocks each) so the round
 // keeps R * s units busy instead of R. s < 2 means no split.
 int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, DeviceState* dev,
               LaunchPlan* plan) {
@@ -312,7 +313,9 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     if (cfg.split_k == 1) return RIDGE_OK;
     const int64_t rem = tiles >= units ? tiles % units : tiles;
     if (rem == 0) return RIDGE_OK;
-    const int64_t s = std::min<int64_t>(std::min<int64_t>(units / rem, 8), num_kb);
+    // Each K range keeps at least kMinSplitBlocks K-blocks: below that the
+    // FP32 partial round-trip costs about what the split saves.
+    const int64_t s = std::min<int64_t>(std::min<int64_t>(units / rem, 8), num_kb / kMinSplitBlocks);
     if (s < 2) return RIDGE_OK;
     plan->dp_tiles = int(tiles - rem);
     plan->sk_tiles = int(rem);

@@ -182,7 +182,7 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     int64_t splits = 1;
     if (t.split_k != 1 && rem > 0)
         splits = std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(units / rem, 8),
-                                                        int64_t(kb)));
+                                                        int64_t(kb) / 4));
     const int64_t dp_tiles = splits >= 2 ? tiles - rem : tiles;
     const int64_t grid_units = std::max(std::min(tiles, units), splits >= 2 ? rem * splits : 0);
     // CTAs actually sharing one SM (a small grid leaves SMs with fewer).

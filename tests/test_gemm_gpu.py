@@ -149,7 +149,7 @@ SPLITK_CASES = [
     ((16, 2048, 4096), (128, 256, 64, 4, 8, 8)),          # skinny M
     ((512, 768, 2048), (256, 256, 64, 4, 4, 8, 2)),       # 2-CTA pairs, 8-way
     ((1000, 1000, 1000), (128, 128, 32, 3, 4, 8)),        # ragged + 2-way
-    ((1280, 2048, 256), (128, 128, 64, 4, 4, 8)),         # whole rounds + split tail
+    ((1280, 2048, 1024), (128, 128, 64, 4, 4, 8)),        # whole rounds + split tail
     ((2048, 2560, 512), (256, 256, 64, 4, 8, 8, 2)),      # pairs: whole rounds + split tail
     ((640, 384, 1024), (64, 128, 64, 4, 4, 1)),           # M=64 UMMA rows
 ]
