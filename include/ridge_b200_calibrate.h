@@ -26,17 +26,19 @@ extern "C" {
 int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, double* clock_hz);
 
 /* TMA tile-load bandwidth: `ctas_per_sm` CTAs per SM each keep `depth` boxes of
- * box_rows x 64 FP16 (box_rows*128 bytes) in flight, reading a K-major tensor of
+ * box_rows x box_cols FP16 in flight, reading a K-major tensor of
  * about tensor_bytes (L2-resident when small, HBM-streaming when large).
  * private_regions = 0: CTAs sweep the tensor together, so many SMs read the
  * same box at the same moment (the pattern of GEMM operand panels shared
  * through L2); 1: each CTA cycles over 16 boxes of its own (no shared bytes).
  * issuers = threads per CTA issuing loads, each with its own `depth` slots.
+ * box_cols = FP16 columns per box row: 64 (128 B, 128B swizzle: BK=64 tiles)
+ * or 32 (64 B, 64B swizzle: BK=32 tiles).
  * Returns bytes per SM cycle per SM and aggregate bytes per second. Replaces
  * cal-hbm-bw.cu:22-109 and the latency surface of cal-latency.cu:56-256. */
 int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t ctas_per_sm,
-                  int32_t private_regions, int32_t issuers, double* bytes_per_cycle_sm,
-                  double* total_bytes_per_sec);
+                  int32_t private_regions, int32_t issuers, int32_t box_cols,
+                  double* bytes_per_cycle_sm, double* total_bytes_per_sec);
 
 /* Epilogue drain rate, bytes of FP16 C per SM cycle (per SM) and per second
  * (aggregate, optional), for `warps` (4 or 8) warps doing TMEM load -> convert

@@ -118,7 +118,7 @@ SIGNATURES = {
                                   _i64, _i64, _i32, _i32, _vp, C.POINTER(C.c_double)]),
     "ridge_cal_umma": (C.c_int, [_i32, _i32, _i32, C.POINTER(C.c_double),
                                  C.POINTER(C.c_double)]),
-    "ridge_cal_tma": (C.c_int, [_i64, _i32, _i32, _i32, _i32, _i32, C.POINTER(C.c_double),
+    "ridge_cal_tma": (C.c_int, [_i64, _i32, _i32, _i32, _i32, _i32, _i32, C.POINTER(C.c_double),
                                 C.POINTER(C.c_double)]),
     "ridge_cal_epi": (C.c_int, [_i32, _i64, _i32, C.POINTER(C.c_double),
                                 C.POINTER(C.c_double)]),

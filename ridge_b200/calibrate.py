@@ -55,9 +55,10 @@ def umma(m, n, iters=20000):
     return cyc.value, hz.value
 
 
-def tma(tensor_bytes, box_rows, depth, ctas=1, private=0, issuers=1):
+def tma(tensor_bytes, box_rows, depth, ctas=1, private=0, issuers=1, box_cols=64):
     per_sm, total = C.c_double(), C.c_double()
-    check(lib.ridge_cal_tma(tensor_bytes, box_rows, depth, ctas, private, issuers, C.byref(per_sm),
+    check(lib.ridge_cal_tma(tensor_bytes, box_rows, depth, ctas, private, issuers, box_cols,
+                            C.byref(per_sm),
                             C.byref(total)),
           "ridge_cal_tma")
     return per_sm.value, total.value
@@ -235,6 +236,11 @@ def calibrate(verbose=True):
     per_sm4, tot4 = tma(32 << 20, 128, 2, 1, 0, 4)
     per_sm8, tot8 = tma(32 << 20, 128, 1, 1, 0, 8)
     res["tmaBytesPerCycle"] = per_sm4
+    # BK=32 tiles load 64-byte-wide boxes (64B swizzle)
+    per_sm32, _ = tma(32 << 20, 128, 2, 1, 0, 4, 32)
+    res["tmaBoxCycles32Ratio"] = per_sm4 / (2.0 * per_sm32)
+    log("tma fill, 4 issuers, 64-byte boxes: %.1f B/cycle/SM -> box time ratio %.2f" % (
+        per_sm32, res["tmaBoxCycles32Ratio"]))
     raw["tma_l2_box128_d1_issuers8"] = [per_sm8, tot8]
     log("tma fill, 4 issuers %.1f B/cycle/SM, 8 issuers %.1f" % (per_sm4, per_sm8))
     raw["copy_bytes_per_sec"] = copy_bw()

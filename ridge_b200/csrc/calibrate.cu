@@ -111,7 +111,7 @@ __global__ void cal_umma_kernel(int m, int n, int iters, unsigned long long* cyc
 // an L2-resident tensor is shared by all SMs while a large one streams.
 __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int depth, int box_bytes,
                                int loads, int box_rows, int k_boxes, int row_tiles, int private_regions,
-                               int issuers, unsigned long long* cycles, int* err) {
+                               int issuers, int box_cols, unsigned long long* cycles, int* err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -137,11 +137,11 @@ __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int dept
             // CTA b cycles over its own 16 boxes: row tile b % row_tiles, K
             // segment b / row_tiles (no two CTAs read the same bytes).
             const int seg = int(blockIdx.x) / row_tiles;
-            kx = ((seg * 16 + (i & 15)) % k_boxes) * 64;
+            kx = ((seg * 16 + (i & 15)) % k_boxes) * box_cols;
             ry = (int(blockIdx.x) % row_tiles) * box_rows;
         } else {
             const int g = int(blockIdx.x) * loads + i;
-            kx = (g % k_boxes) * 64;
+            kx = (g % k_boxes) * box_cols;
             ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
         }
         tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
@@ -333,10 +333,10 @@ int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, 
 }
 
 int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t ctas_per_sm,
-                  int32_t private_regions, int32_t issuers, double* bytes_per_cycle_sm,
-                  double* total_bytes_per_sec) {
+                  int32_t private_regions, int32_t issuers, int32_t box_cols,
+                  double* bytes_per_cycle_sm, double* total_bytes_per_sec) {
     if (!bytes_per_cycle_sm || !total_bytes_per_sec || depth < 1 || issuers < 1 ||
-        issuers * depth > 16 ||
+        issuers * depth > 16 || !(box_cols == 32 || box_cols == 64) ||
         !(box_rows == 64 || box_rows == 128 || box_rows == 256) || ctas_per_sm < 1 ||
         tensor_bytes < (1 << 20))
         return RIDGE_EINVAL;
@@ -355,15 +355,16 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     CUtensorMap map;
     cuuint64_t dims[2] = {cuuint64_t(kcols), cuuint64_t(rows)};
     cuuint64_t strides[1] = {cuuint64_t(kcols * 2)};
-    cuuint32_t box[2] = {64, cuuint32_t(box_rows)};
+    cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
     cuuint32_t es[2] = {1, 1};
     if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf, dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE,
+            box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
         cudaFree(buf);
         return RIDGE_EINVAL;
     }
-    const int box_bytes = box_rows * 128;
+    const int box_bytes = box_rows * box_cols * 2;
     const int slots = depth * issuers;
     if (slots * box_bytes + 1024 > 232448 || ctas_per_sm * (slots * box_bytes + 2048) > 233472) {
         cudaFree(buf);
@@ -387,18 +388,18 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
-    const int k_boxes = int(kcols / 64), row_tiles = int(rows / box_rows);
+    const int k_boxes = int(kcols / box_cols), row_tiles = int(rows / box_rows);
     if (private_regions && int64_t(row_tiles) * (k_boxes / 16) < grid) {
         cudaFree(d);
         cudaFree(buf);
         return RIDGE_EINVAL;  // tensor too small for one private region per CTA
     }
     cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, std::min(loads, 64 * issuers),
-                                       box_rows, k_boxes, row_tiles, private_regions, issuers, d,
-                                       err);
+                                       box_rows, k_boxes, row_tiles, private_regions, issuers,
+                                       box_cols, d, err);
     cudaEventRecord(e0);
     cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, loads, box_rows, k_boxes,
-                                       row_tiles, private_regions, issuers, d, err);
+                                       row_tiles, private_regions, issuers, box_cols, d, err);
     cudaEventRecord(e1);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();

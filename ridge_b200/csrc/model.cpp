@@ -98,6 +98,17 @@ double dram_bytes(int64_t M, int64_t N, int64_t K, int BM, int BN, int groupM, i
     return total;
 }
 
+// Smooth maximum (p-norm) of two times that overlap: equals the larger when
+// one dominates, and exceeds it when both are close -- two limits that each
+// nearly bind do not overlap perfectly. It also keeps the losing limit in the
+// prediction, so configs held to the same bound are still ordered.
+double soft_max(double a, double b) {
+    constexpr double kP = 4.0;
+    const double m = std::max(a, b);
+    if (m <= 0.0) return 0.0;
+    return m * std::pow(std::pow(a / m, kP) + std::pow(b / m, kP), 1.0 / kP);
+}
+
 }  // namespace
 
 extern "C" {
@@ -194,7 +205,7 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     // The SM keeps about four boxes in flight in all (one CTA with four
     // issuing threads already reaches it), so resident CTAs share that
     // budget exactly like they share the tensor core.
-    const double t_stage = std::max(t_mma, t_fill) * resident / hw->pipeline_efficiency;
+    const double t_stage = soft_max(t_mma, t_fill) * resident / hw->pipeline_efficiency;
     // A ring slot refills only after its MMAs finish: the load then waits
     // behind the pair's current box (t_fill) and travels for the unloaded
     // latency, so `stages` slots must cover (latency + t_fill + t_stage).
@@ -206,7 +217,7 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     const double epi_bpc = t.warps == 8 ? hw->epi_bytes_per_cycle_w8 : hw->epi_bytes_per_cycle_w4;
     const double t_epi = c_bytes_tile / epi_bpc;
     auto tile_period = [&](double t_main) {
-        return info.acc_buffers >= 2 ? std::max(t_main, t_epi) : t_main + t_epi;
+        return info.acc_buffers >= 2 ? soft_max(t_main, t_epi) : t_main + t_epi;
     };
     const double dp_rounds = std::ceil(double(dp_tiles) / double(std::min(units, std::max<int64_t>(dp_tiles, 1))));
     const double dp_per_unit = dp_tiles > 0 ? std::ceil(double(dp_tiles) / double(std::min(tiles, units))) : 0.0;
@@ -217,7 +228,9 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
         // One K range of 1/splits, then the owner folds in splits - 1 FP32
         // partial tiles (read at the fill rate) before its epilogue.
         const double partial_bytes = double(g.rows_per_cta) * t.BN * 4.0;
-        t_sk = std::ceil(kb / double(splits)) * t_period +
+        // The owner cannot reduce before the other splits have written their
+        // FP32 partials (twice the bytes of an FP16 tile, at the drain rate).
+        t_sk = std::ceil(kb / double(splits)) * t_period + partial_bytes / epi_bpc +
                double(splits - 1) * partial_bytes / (2.0 * epi_bpc) + t_epi;
         t_unit += t_sk;
     } else if (info.acc_buffers >= 2 && dp_per_unit > 0) {
@@ -243,7 +256,7 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     p.peak_tensor_tflops = peak_flops_per_cycle_sm * hw->clock_hz * hw->num_sms / 1e12;
     p.compute_tflops = flops / compute_sec / 1e12;
     p.hbm_tflops = flops / hbm_sec / 1e12;
-    p.predicted_seconds = std::max(compute_sec, hbm_sec);
+    p.predicted_seconds = soft_max(compute_sec, hbm_sec);
     p.predicted_tflops = flops / p.predicted_seconds / 1e12;
     p.dram_bytes = a_b_reads + c_write;
     p.arithmetic_intensity = flops / p.dram_bytes;
