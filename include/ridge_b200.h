@@ -322,9 +322,9 @@ int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
 
 /*
  * Times one config on caller-owned device buffers with CUDA events on
- * `stream`: `warmup` launches, a short probe, then an adaptive run of at least
- * `iters` back-to-back launches (about 20 ms of work, at most max(400, iters)).
- * *ms_per_launch = mean launch time. Synchronises the stream. Replaces
+ * `stream`: `warmup` launches, a short probe, then three adaptive runs of at
+ * least `iters` back-to-back launches (about 20 ms of work each, at most
+ * max(400, iters)). *ms_per_launch = mean launch time of the fastest run. Synchronises the stream. Replaces
  * timeTflops (bench/measure.cu:121-150).
  */
 int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, void* C,

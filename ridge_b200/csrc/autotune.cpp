@@ -12,7 +12,7 @@
 //
 // Timer: the reference's measure.cu:121-150 method -- warm-up launches, a short
 // probe to size the run, then an adaptive number of back-to-back launches
-// between two events.
+// between two events -- repeated three times, keeping the fastest.
 
 #include <cuda_runtime.h>
 
@@ -30,6 +30,7 @@ namespace {
 
 constexpr double kTargetSeconds = 0.02;  // timed work per candidate
 constexpr int kMaxIters = 400;
+constexpr int kRepeats = 3;  // timed runs per candidate; the fastest counts
 
 struct Job {
     int shape;
@@ -66,17 +67,23 @@ int time_on_stream(const ridge_tile_config* cfg, const void* A, const void* B, v
     cudaEventElapsedTime(&probe, e0, e1);
     int iters = int(kTargetSeconds * 1e3 / std::max(double(probe) / 3.0, 1e-4));
     iters = std::min(std::max(iters, std::max(1, min_iters)), std::max(kMaxIters, min_iters));
-    cudaEventRecord(e0, s);
-    for (int i = 0; i < iters; ++i) {
-        st = ridge_gemm_launch(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, s);
-        if (st != RIDGE_OK) return st;
+    // Best of kRepeats timed runs: on a power-capped part one short run can
+    // land on a clock dip; the fastest run is the config's sustainable rate.
+    double best = 1e30;
+    for (int rep = 0; rep < kRepeats; ++rep) {
+        cudaEventRecord(e0, s);
+        for (int i = 0; i < iters; ++i) {
+            st = ridge_gemm_launch(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, s);
+            if (st != RIDGE_OK) return st;
+        }
+        cudaEventRecord(e1, s);
+        ce = cudaEventSynchronize(e1);
+        if (ce != cudaSuccess) return int(ce);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        best = std::min(best, double(ms) / iters);
     }
-    cudaEventRecord(e1, s);
-    ce = cudaEventSynchronize(e1);
-    if (ce != cudaSuccess) return int(ce);
-    float ms = 0.f;
-    cudaEventElapsedTime(&ms, e0, e1);
-    *ms_out = double(ms) / iters;
+    *ms_out = best;
     return RIDGE_OK;
 }
 
