@@ -205,6 +205,8 @@ typedef struct ridge_hw {
     double hbm_bytes_per_sec;        /* [CAL] whole-GPU HBM read bandwidth (TMA streaming) */
     double tma_box_cycles;           /* [CAL] cycles per TMA box per issuing thread, 4 threads issuing */
     double pipeline_efficiency;      /* [CAL] steady-state mainloop rate / ideal, from a calibration GEMM */
+    double tile_overhead_cycles;     /* [CAL] per-tile turnover beyond the drain, one-CTA tiles */
+    double pair_tile_overhead_cycles;/* [CAL] the same for 2-CTA pair tiles */
     double c_write_bytes_per_sec;    /* [CAL] epilogue write rate of a C far larger than L2 */
     double epi_bytes_per_cycle_w4;   /* [CAL] C bytes/cycle/SM drained by 4 epilogue warps */
     double epi_bytes_per_cycle_w8;   /* [CAL] same with 8 epilogue warps */

@@ -126,6 +126,51 @@ def pipeline_efficiency(res):
     return min(1.0, meas / ideal), meas, ideal
 
 
+TURN_SHAPE = (6144, 6144, 64)
+
+
+def _hw_from(res):
+    from ._native import HwC
+    from .model import HW_KEYS
+    hw = HwC()
+    lib.ridge_hw_b200(C.byref(hw))
+    for k, f in HW_KEYS.items():
+        if k in res:
+            setattr(hw, f, type(getattr(hw, f))(res[k]))
+    return hw
+
+
+def _time_tflops(M, N, K, cfg):
+    import torch
+
+    from .gemm import synthetic_inputs
+    a, b = synthetic_inputs(M, N, K)
+    c = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    ms = C.c_double()
+    cc = cfg.to_c()
+    check(lib.ridge_time_gemm(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, K,
+                              K, N, 10, 50, torch.cuda.current_stream().cuda_stream,
+                              C.byref(ms)), "ridge_time_gemm")
+    return ms.value
+
+
+def tile_overhead(res, cfg_tuple):
+    """Per-tile turnover cost: a K=64 GEMM (one K-block per tile, outside the
+    validation sweep) is nothing but tile turnovers; whatever its measured time
+    per tile exceeds the model's drain-and-mainloop time is the hand-off cost."""
+    from .gemm import TileConfig
+    from .model import predict
+    M, N, K = TURN_SHAPE
+    cfg = TileConfig(*cfg_tuple)
+    ms = _time_tflops(M, N, K, cfg)
+    hw = _hw_from(res)
+    p = predict(M, N, K, cfg, hw)
+    tiles_per_unit = p["total_tiles"] / min(p["total_tiles"], p["tile_slots"])
+    meas_cycles = (ms * 1e-3 - hw.launch_overhead_sec) * hw.clock_hz / tiles_per_unit
+    model_cycles = (p["predicted_seconds"] - hw.launch_overhead_sec) * hw.clock_hz / tiles_per_unit
+    return max(0.0, meas_cycles - model_cycles), meas_cycles, model_cycles
+
+
 def fit_smem(cycles_by_n, m=128):
     """From cycles(n) of m x n x 16 MMAs: tensor cycles per 128x256 MMA, smem
     bytes/cycle, and whether operand reads overlap (max) or add (sum).
@@ -251,6 +296,15 @@ def calibrate(verbose=True):
                 "tmemColsPerSM": 512, "maxCtasPerSM": 32})
     res["tmaBoxCycles"] = 4 * 128 * 128 / res.pop("tmaBytesPerCycle")
     res["pipelineEfficiency"] = 1.0
+    res["tileOverheadCycles"] = 0.0
+    res["pairTileOverheadCycles"] = 0.0
+    for key, cfg in (("tileOverheadCycles", (128, 256, 64, 4, 8, 8, 1)),
+                     ("pairTileOverheadCycles", (256, 256, 64, 4, 8, 8, 2))):
+        res[key], meas_t, model_t = tile_overhead(res, cfg)
+        raw[key] = {"shape": list(TURN_SHAPE), "config": list(cfg), "measured_tile_cycles": meas_t,
+                    "modelled_tile_cycles_without_overhead": model_t}
+        log("tile turnover %s: %.0f cycles measured vs %.0f modelled -> %s %.0f" % (
+            cfg, meas_t, model_t, key, res[key]))
     eff, meas, ideal = pipeline_efficiency(res)
     res["pipelineEfficiency"] = eff
     raw["calibration_gemm"] = {"shape": list(CAL_GEMM[:3]), "config": CAL_GEMM[3].tag(),

@@ -216,8 +216,13 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     const double c_bytes_tile = double(g.rows_per_cta) * t.BN * 2.0;
     const double epi_bpc = t.warps == 8 ? hw->epi_bytes_per_cycle_w8 : hw->epi_bytes_per_cycle_w4;
     const double t_epi = c_bytes_tile / epi_bpc;
+    // Turning a tile over costs a fixed hand-off on top of the drain (the
+    // accumulator's full/empty barrier round trip; across the two SMs of a
+    // pair); measured on short-K calibration GEMMs.
+    const double t_turn =
+        (g.cg == 2 ? hw->pair_tile_overhead_cycles : hw->tile_overhead_cycles) * resident;
     auto tile_period = [&](double t_main) {
-        return info.acc_buffers >= 2 ? soft_max(t_main, t_epi) : t_main + t_epi;
+        return (info.acc_buffers >= 2 ? soft_max(t_main, t_epi) : t_main + t_epi) + t_turn;
     };
     const double dp_rounds = std::ceil(double(dp_tiles) / double(std::min(units, std::max<int64_t>(dp_tiles, 1))));
     const double dp_per_unit = dp_tiles > 0 ? std::ceil(double(dp_tiles) / double(std::min(tiles, units))) : 0.0;

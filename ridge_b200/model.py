@@ -24,6 +24,8 @@ HW_KEYS = {  # JSON key -> struct field
     "smemMmaOverlap": "smem_mma_overlap", "l2BytesPerSec": "l2_bytes_per_sec",
     "hbmBytesPerSec": "hbm_bytes_per_sec", "tmaBoxCycles": "tma_box_cycles",
     "pipelineEfficiency": "pipeline_efficiency",
+    "tileOverheadCycles": "tile_overhead_cycles",
+    "pairTileOverheadCycles": "pair_tile_overhead_cycles",
     "cWriteBytesPerSec": "c_write_bytes_per_sec", "epiBytesPerCycleW4": "epi_bytes_per_cycle_w4",
     "epiBytesPerCycleW8": "epi_bytes_per_cycle_w8", "tmaLatencyCycles": "tma_latency_cycles",
     "launchOverheadSec": "launch_overhead_sec", "l2Bytes": "l2_bytes",
