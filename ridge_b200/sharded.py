@@ -14,7 +14,7 @@ slabs and re-lays it out into row-major C with ridge_slabs_to_rowmajor.
 One process per GPU (torchrun); the reference is single-GPU, so this is the
 B200 build's own multi-GPU mode.
 
-    torchrun --nproc-per-node 8 -m ridge_b200.sharded --m 16384 --n 16384 --k 16384
+    torchrun --nproc-per-node 8 -m ridge_b200.sharded --shape 16384x16384x16384 [--gather]
 """
 
 from __future__ import annotations
@@ -100,9 +100,7 @@ def main(argv=None):
 
     from .gemm import fill_lcg
     ap = argparse.ArgumentParser()
-    ap.add_argument("--m", type=int, default=16384)
-    ap.add_argument("--n", type=int, default=16384)
-    ap.add_argument("--k", type=int, default=16384)
+    ap.add_argument("--shape", default="16384x16384x16384", help="MxNxK")
     ap.add_argument("--config", default="256,256,64,5,4,8,2",
                     help="BM,BN,BK,stages,warps,groupM,cta_group")
     ap.add_argument("--steps", type=int, default=10)
@@ -117,7 +115,7 @@ def main(argv=None):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     cfg = TileConfig(*[int(x) for x in a.config.split(",")])
-    M, N, K = a.m, a.n, a.k
+    M, N, K = (int(x) for x in a.shape.lower().split("x"))
     n0, ns = slab_bounds(N, world, rank)
     A = torch.empty((M, K), dtype=torch.float16, device=dev)
     st = fill_lcg(A, 0)
