@@ -119,3 +119,18 @@ def test_unit_inputs_range_and_stream():
     # B continues A's stream: drawing A and B as one run gives the same bits
     both, _ = oracle.unit_inputs(16 * 32 + 8 * 32, 0, 1, seed=0)
     assert np.array_equal(both.ravel(), np.concatenate([a.ravel(), b.ravel()]))
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="reference library not built here")
+def test_reference_a100_model_matches_its_hand_derived_example():
+    """The reference's own model (src/model.cpp, linked into oracle/_ref) on its
+    worked example, checked against the hand-derived values of
+    test/test-model.cpp:47-101 -- pins the parity shim."""
+    p = oracle.Reference().predict_a100(4096, 4096, 4096, 128, 128, 32, 64, 64, 3, 128)
+    assert p["tComputeCycles"] == pytest.approx(512.0)
+    assert p["tSmemCycles"] == pytest.approx(256.0)
+    assert p["ctasPerSM"] == 3
+    assert p["waveEfficiency"] == pytest.approx(1024.0 / 1296.0)
+    assert p["envelopeEfficiency"] == pytest.approx(0.975248, abs=1e-6)
+    assert p["predictedTFLOPS"] == pytest.approx(120.158068, abs=1e-4)
+    assert p["bottleneck"] == 1  # Smem
