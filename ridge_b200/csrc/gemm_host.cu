@@ -117,14 +117,29 @@ int make_operand_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t co
                      int box_rows, int bk) {
     auto enc = tensor_map_encoder();
     if (!enc) return RIDGE_ENOTSUP;
-    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
-    cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
-    cuuint32_t box[2] = {cuuint32_t(bk), cuuint32_t(box_rows)};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r;
+    if (bk <= 64) {
+        cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+        cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+        cuuint32_t box[2] = {cuuint32_t(bk), cuuint32_t(box_rows)};
+        cuuint32_t estr[2] = {1, 1};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        // BK=128: view the operand as (64 columns of an atom) x rows x (K / 64
+        // atoms), atom stride 128 B, and load bk/64 atoms per box; the box lands
+        // atom-major in shared memory (rows x 128 B per atom), the layout the
+        // 128B-swizzled UMMA descriptors read. Needs K to be a multiple of 64.
+        cuuint64_t dims[3] = {64, cuuint64_t(rows), cuuint64_t(cols / 64)};
+        cuuint64_t strides[2] = {cuuint64_t(ld) * 2, 128};
+        cuuint32_t box[3] = {64, cuuint32_t(box_rows), cuuint32_t(bk / 64)};
+        cuuint32_t estr[3] = {1, 1, 1};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     return r == CUDA_SUCCESS ? RIDGE_OK : RIDGE_EINVAL;
 }
 
@@ -189,14 +204,15 @@ int ctas_per_sm(const KernelEntry& e, int stages) {
     return std::max(0, std::min(std::min(by_smem, by_tmem), by_threads));
 }
 
-// The registered table: the full grid BM, BN in {64,128,256}, BK in {32,64},
-// stages in {2..5}, warps in {4,8}, groupM 8, minus the points that overflow
-// shared memory (valid-config filter); BM=256 appears twice, as the 2-CTA pair
+// The registered table: the full grid BM, BN in {64,128,256}, BK in {32,64}
+// (BASELINE) widened with BK=128 (two K atoms per TMA box, half the boxes per
+// unit of MMA work), stages in {2..5}, warps in {4,8}, groupM 8, minus the
+// points that overflow shared memory; BM=256 appears twice, as the 2-CTA pair
 // and as the single-CTA form.
 const std::vector<ridge_tile_config>& variant_table() {
     static const std::vector<ridge_tile_config> table = [] {
         std::vector<ridge_tile_config> t;
-        const int bms[] = {64, 128, 256}, bns[] = {64, 128, 256}, bks[] = {32, 64};
+        const int bms[] = {64, 128, 256}, bns[] = {64, 128, 256}, bks[] = {32, 64, 128};
         const int stages[] = {2, 3, 4, 5}, warps[] = {4, 8};
         for (int bm : bms)
             for (int bn : bns)
@@ -508,6 +524,7 @@ int ridge_config_valid_for_shape(const ridge_tile_config* cfg, int64_t M, int64_
     if (lda < K || ldb < K || ldc < N) return RIDGE_EINVAL;
     if (lda % 8 != 0 || ldb % 8 != 0) return RIDGE_EINVAL;  // TMA: strides multiple of 16 B
     if (lda < 8 || ldb < 8) return RIDGE_EINVAL;
+    if (cfg->BK == 128 && K % 64 != 0) return RIDGE_EINVAL;  // whole 64-wide K atoms
     return RIDGE_OK;
 }
 

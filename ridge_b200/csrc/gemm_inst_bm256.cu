@@ -19,6 +19,12 @@ void register_bm256(std::vector<KernelEntry>& out) {
     RIDGE_1CTA(256, 32, 8);
     RIDGE_1CTA(256, 64, 4);
     RIDGE_1CTA(256, 64, 8);
+    RIDGE_1CTA(64, 128, 4);
+    RIDGE_1CTA(64, 128, 8);
+    RIDGE_1CTA(128, 128, 4);
+    RIDGE_1CTA(128, 128, 8);
+    RIDGE_1CTA(256, 128, 4);
+    RIDGE_1CTA(256, 128, 8);
 }
 
 #undef RIDGE_1CTA

@@ -59,7 +59,8 @@ struct GemmTraits {
     static constexpr int BM = BM_, BN = BN_, BK = BK_, kEpiWarps = WARPS_, CG = CG_;
     static_assert(BM == 64 || BM == 128 || BM == 256, "BM must be 64, 128 or 256");
     static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
-    static_assert(BK == 32 || BK == 64, "BK must be 32 or 64 (one 64B or 128B swizzle row)");
+    static_assert(BK == 32 || BK == 64 || BK == 128,
+                  "BK must be 32 or 64 (one 64B / 128B swizzle row) or 128 (two 128B atoms)");
     static_assert(WARPS_ == 4 || WARPS_ == 8, "epilogue warps must be 4 or 8");
     static_assert(CG == 1 || (CG == 2 && BM == 256), "the 2-CTA variant computes 256-row tiles");
 
@@ -68,7 +69,11 @@ struct GemmTraits {
     static constexpr int kUmmaM = CG == 2 ? 256 : (BM == 64 ? 64 : 128);
     static constexpr int kMHalves = (CG == 1 && BM == 256) ? 2 : 1;  // MMAs per K-step along M
     static constexpr int kUmmaK = 16;                      // K per tcgen05.mma (FP16)
-    static constexpr int kSwizzle = BK * 2;                // bytes per operand row
+    static constexpr int kSwizzle = BK >= 64 ? 128 : BK * 2;  // bytes per swizzle row
+    // K atoms per stage: a 128B-swizzled row holds 64 FP16 of K, so a BK=128
+    // stage is two atoms, each (rows x 128 B), loaded by one 3-D TMA box.
+    static constexpr int kAtoms = BK >= 64 ? BK / 64 : 1;
+    static constexpr int kAtomK = BK / kAtoms;               // K per atom
     static constexpr int kTileABytes = kRowsA * BK * 2;
     static constexpr int kTileBBytes = kRowsB * BK * 2;
     static constexpr int kStageBytes = kTileABytes + kTileBBytes;
@@ -273,22 +278,24 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                         break;
                     }
                     const uint32_t sa = base + stage * T::kStageBytes;
-                    if constexpr (CG == 1) {
-                        if (loads_a) {
-                            mbar_arrive_expect_tx(full_bar(stage), T::kStageBytes);
-                            tma_load_2d(sa, &tmap_a, full_bar(stage), kb * BK, a_row);
-                        } else {
-                            tma_load_2d(sa + T::kTileABytes, &tmap_b, full_bar(stage), kb * BK,
-                                        b_row);
-                        }
+                    const uint32_t fb =
+                        CG == 1 ? full_bar(stage) : leader_full0 + 8u * uint32_t(stage);
+                    if (loads_a && leader)
+                        mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
+                    const uint32_t dst = loads_a ? sa : sa + T::kTileABytes;
+                    const void* map = loads_a ? static_cast<const void*>(&tmap_a)
+                                              : static_cast<const void*>(&tmap_b);
+                    const int row = loads_a ? a_row : b_row;
+                    if constexpr (T::kAtoms == 1) {
+                        if constexpr (CG == 1)
+                            tma_load_2d(dst, map, fb, kb * BK, row);
+                        else
+                            tma_load_2d_pair(dst, map, fb, kb * BK, row);
                     } else {
-                        const uint32_t fb = leader_full0 + 8u * stage;
-                        if (loads_a) {
-                            if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
-                            tma_load_2d_pair(sa, &tmap_a, fb, kb * BK, a_row);
-                        } else {
-                            tma_load_2d_pair(sa + T::kTileABytes, &tmap_b, fb, kb * BK, b_row);
-                        }
+                        if constexpr (CG == 1)
+                            tma_load_3d(dst, map, fb, 0, row, kb * T::kAtoms);
+                        else
+                            tma_load_3d_pair(dst, map, fb, 0, row, kb * T::kAtoms);
                     }
                 }
                 ++issued;
@@ -338,11 +345,18 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 const uint32_t sb = sa + T::kTileABytes;
 #pragma unroll
                 for (int kk = 0; kk < BK / T::kUmmaK; ++kk) {
-                    const uint64_t bdesc = make_smem_desc<T::kSwizzle>(sb + kk * T::kUmmaK * 2);
+                    // K step kk lives in atom kk / (atom K / 16), at byte
+                    // offset 32 * (kk mod that) inside the atom's rows.
+                    constexpr int kStepsPerAtom = T::kAtomK / T::kUmmaK;
+                    const int atom = kk / kStepsPerAtom;
+                    const int in_atom = (kk % kStepsPerAtom) * T::kUmmaK * 2;
+                    const uint64_t bdesc = make_smem_desc<T::kSwizzle>(
+                        sb + atom * T::kRowsB * T::kSwizzle + in_atom);
 #pragma unroll
                     for (int h = 0; h < T::kMHalves; ++h) {
                         const uint64_t adesc = make_smem_desc<T::kSwizzle>(
-                            sa + h * 128 * BK * 2 + kk * T::kUmmaK * 2);
+                            sa + atom * T::kRowsA * T::kSwizzle + h * 128 * T::kSwizzle +
+                            in_atom);
                         umma_f16<CG>(d_base + h * BN, adesc, bdesc, T::kIdesc,
                                      (kb > w.kb0 || kk > 0) ? 1u : 0u);
                     }

@@ -177,6 +177,25 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap,
         : "memory");
 }
 
+// 3-D tiled bulk-tensor load: used for BK=128 stages, where one box carries
+// two 64-element K atoms (coordinates: column in atom, row, atom index).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int x,
+                                            int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap, uint32_t bar,
+                                                 int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // 2-D tiled bulk-tensor store shared -> global, tracked by bulk async-groups.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {
     asm volatile(

@@ -41,6 +41,10 @@ CONFIGS = [
     (256, 256, 64, 4, 8, 8, 2),
     (256, 64, 32, 3, 4, 3, 2),
     (256, 128, 32, 2, 8, 8, 1),   # single-CTA 256-row tile
+    (128, 128, 128, 3, 4, 8),     # BK=128: two K atoms per TMA box (3-D map)
+    (256, 128, 128, 4, 4, 8, 2),
+    (256, 256, 128, 2, 8, 8, 1),
+    (64, 256, 128, 3, 4, 4),
 ]
 
 
@@ -200,3 +204,17 @@ def test_caller_workspace_launch():
         torch.cuda.synchronize()
         assert rb.device_error() == 0
         assert_close(to_host_bits(c), ref, "caller workspace")
+
+
+@pytest.mark.parametrize("shape", [(200, 136, 192), (129, 257, 64), (300, 520, 1088)],
+                         ids=lambda s: "%dx%dx%d" % s)
+@pytest.mark.parametrize("c", [CONFIGS[11], CONFIGS[12], CONFIGS[13], CONFIGS[14]],
+                         ids=lambda c: "x".join(map(str, c)))
+def test_bk128_tails(shape, c):
+    """BK=128 stages with M/N tails and a K that ends mid-stage (K = 64 mod 128)."""
+    M, N, K = shape
+    a, b = oracle.unit_inputs(M, N, K, seed=9)
+    ref = oracle.gemm_f64(a, b)
+    cfg = _cfg(*c)
+    out = run_gemm(cfg, to_dev(a), to_dev(b), M, N, K)
+    assert_close(to_host_bits(out), ref, "%s %dx%dx%d" % (cfg.tag(), M, N, K))

@@ -38,7 +38,7 @@ def _smem_bytes(bm, bn, bk, s, w, cg):
 
 
 def test_variant_table_is_the_valid_grid():
-    """BM, BN in {64,128,256} x BK in {32,64} x stages 2..5 x warps {4,8}, with
+    """BM, BN in {64,128,256} x BK in {32,64} (widened with 128) x stages 2..5 x warps {4,8}, with
     BM=256 both as a 2-CTA pair and as one CTA: every point whose shared memory
     fits in 227 KB is registered, every other point is refused. The four grid
     points whose operand ring alone overflows are among the refused."""
@@ -49,7 +49,7 @@ def test_variant_table_is_the_valid_grid():
     expected = set()
     for bm in (64, 128, 256):
         for bn in (64, 128, 256):
-            for bk in (32, 64):
+            for bk in (32, 64, 128):
                 for s in (2, 3, 4, 5):
                     for w in (4, 8):
                         for cg in ((1, 2) if bm == 256 else (1,)):
@@ -110,3 +110,10 @@ def test_launch_rejects_bad_arguments_before_touching_a_device():
 def test_status_strings():
     for s in (0, -1, -2, -3, -4, -5):
         assert lib.ridge_status_string(s)
+
+
+def test_bk128_needs_whole_k_atoms():
+    cfg = TileConfig(128, 128, 128, 3, 4, 8)
+    assert rb.config_ok(cfg)
+    assert rb.valid_for_shape(cfg, 256, 256, 192)
+    assert not rb.valid_for_shape(cfg, 256, 256, 200)
