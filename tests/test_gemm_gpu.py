@@ -44,7 +44,7 @@ CONFIGS = [
     (128, 128, 128, 3, 4, 8),     # BK=128: two K atoms per TMA box (3-D map)
     (256, 128, 128, 4, 4, 8, 2),
     (256, 256, 128, 3, 8, 8, 2),
-    (64, 256, 128, 3, 4, 4),
+    (64, 256, 128, 2, 4, 4),
 ]
 
 

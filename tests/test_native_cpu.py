@@ -117,3 +117,16 @@ def test_bk128_needs_whole_k_atoms():
     assert rb.config_ok(cfg)
     assert rb.valid_for_shape(cfg, 256, 256, 192)
     assert not rb.valid_for_shape(cfg, 256, 256, 200)
+
+
+def test_gpu_test_configs_are_valid():
+    """Every tile config the GPU parity tests launch is a valid config (so a
+    typo fails here, on CPU, not on a GPU box)."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location(
+        "gemm_gpu_cases", Path(__file__).parent / "test_gemm_gpu.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    for c in mod.CONFIGS + [c for _, c in mod.SPLITK_CASES]:
+        assert rb.config_ok(TileConfig(*c)), c
