@@ -33,7 +33,8 @@ int ridge_cal_umma(int32_t m, int32_t n, int32_t iters, double* cycles_per_mma, 
  * through L2); 1: each CTA cycles over 16 boxes of its own (no shared bytes).
  * issuers = threads per CTA issuing loads, each with its own `depth` slots.
  * box_cols = FP16 columns per box row: 64 (128 B, 128B swizzle: BK=64 tiles)
- * or 32 (64 B, 64B swizzle: BK=32 tiles).
+ * or 32 (64 B, 64B swizzle: BK=32 tiles), or 128 (two 128-byte atoms per 3-D
+ * box: BK=128 tiles).
  * Returns bytes per SM cycle per SM and aggregate bytes per second. Replaces
  * cal-hbm-bw.cu:22-109 and the latency surface of cal-latency.cu:56-256. */
 int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t ctas_per_sm,

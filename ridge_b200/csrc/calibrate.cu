@@ -144,7 +144,10 @@ __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int dept
             kx = (g % k_boxes) * box_cols;
             ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
         }
-        tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
+        if (box_cols == 128)
+            tma_load_3d(base + uint32_t(s * box_bytes), &map, b, 0, ry, kx / 64);
+        else
+            tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
     }
     for (int j = std::max(0, mine - depth); j < mine; ++j)
         mbar_wait(smem_u32(&bars[lane * depth + j % depth]), uint32_t((j / depth) & 1), nullptr,
@@ -336,7 +339,7 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
                   int32_t private_regions, int32_t issuers, int32_t box_cols,
                   double* bytes_per_cycle_sm, double* total_bytes_per_sec) {
     if (!bytes_per_cycle_sm || !total_bytes_per_sec || depth < 1 || issuers < 1 ||
-        issuers * depth > 16 || !(box_cols == 32 || box_cols == 64) ||
+        issuers * depth > 16 || !(box_cols == 32 || box_cols == 64 || box_cols == 128) ||
         !(box_rows == 64 || box_rows == 128 || box_rows == 256) || ctas_per_sm < 1 ||
         tensor_bytes < (1 << 20))
         return RIDGE_EINVAL;
@@ -356,11 +359,23 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
     cuuint64_t dims[2] = {cuuint64_t(kcols), cuuint64_t(rows)};
     cuuint64_t strides[1] = {cuuint64_t(kcols * 2)};
     cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
-    cuuint32_t es[2] = {1, 1};
-    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf, dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE,
-            box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult er;
+    if (box_cols == 128) {
+        // two 64-column atoms per box, the GEMM's BK=128 map (see gemm_host.cu)
+        cuuint64_t d3[3] = {64, cuuint64_t(rows), cuuint64_t(kcols / 64)};
+        cuuint64_t s3[2] = {cuuint64_t(kcols * 2), 128};
+        cuuint32_t b3[3] = {64, cuuint32_t(box_rows), 2};
+        er = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, buf, d3, s3, b3, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        er = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf, dims, strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (er != CUDA_SUCCESS) {
         cudaFree(buf);
         return RIDGE_EINVAL;
     }
