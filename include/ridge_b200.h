@@ -205,6 +205,7 @@ typedef struct ridge_hw {
     double hbm_bytes_per_sec;        /* [CAL] whole-GPU HBM read bandwidth (TMA streaming) */
     double tma_box_cycles;           /* [CAL] cycles per TMA box per issuing thread, 4 threads issuing */
     double tma_box2_ratio;           /* [CAL] cost of a two-atom (BK=128) box / a one-atom box */
+    double tma_box32_ratio;          /* [CAL] cost of a 64-byte-wide (BK=32) box / a one-atom box */
     double pipeline_efficiency;      /* [CAL] steady-state mainloop rate / ideal, from a calibration GEMM */
     double tile_overhead_cycles;     /* [CAL] per-tile turnover beyond the drain, one-CTA tiles */
     double pair_tile_overhead_cycles;/* [CAL] the same for 2-CTA pair tiles */

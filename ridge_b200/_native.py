@@ -44,6 +44,7 @@ class HwC(C.Structure):
                 ("smem_bytes_per_cycle", C.c_double), ("smem_mma_overlap", C.c_double),
                 ("l2_bytes_per_sec", C.c_double), ("hbm_bytes_per_sec", C.c_double),
                 ("tma_box_cycles", C.c_double), ("tma_box2_ratio", C.c_double),
+                ("tma_box32_ratio", C.c_double),
                 ("pipeline_efficiency", C.c_double),
                 ("tile_overhead_cycles", C.c_double), ("pair_tile_overhead_cycles", C.c_double),
                 ("c_write_bytes_per_sec", C.c_double),

@@ -284,7 +284,7 @@ def calibrate(verbose=True):
     # BK=32 tiles load 64-byte-wide boxes (64B swizzle)
     per_sm32, _ = tma(32 << 20, 128, 2, 1, 0, 4, 32)
     res["tmaBoxCycles32Ratio"] = per_sm4 / (2.0 * per_sm32)
-    per_sm128, _ = tma(32 << 20, 128, 2, 1, 0, 4, 128)
+    per_sm128, _ = tma(32 << 20, 128, 1, 1, 0, 4, 128)
     res["tmaBoxCycles128Ratio"] = 2.0 * per_sm4 / per_sm128
     log("tma fill, 4 issuers, two-atom boxes: %.1f B/cycle/SM -> box time ratio %.2f" % (
         per_sm128, res["tmaBoxCycles128Ratio"]))

@@ -144,6 +144,7 @@ int ridge_hw_b200(ridge_hw* h) {
     h->hbm_bytes_per_sec = 6.5e12;
     h->tma_box_cycles = 1030.0;
     h->tma_box2_ratio = 1.0;
+    h->tma_box32_ratio = 1.0;
     h->pipeline_efficiency = 0.9;
     h->tile_overhead_cycles = 0.0;
     h->pair_tile_overhead_cycles = 0.0;
@@ -195,6 +196,7 @@ int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t er
                {"hbmBytesPerSec", &h.hbm_bytes_per_sec},
                {"tmaBoxCycles", &h.tma_box_cycles},
                {"tmaBoxCycles128Ratio", &h.tma_box2_ratio},
+               {"tmaBoxCycles32Ratio", &h.tma_box32_ratio},
                {"pipelineEfficiency", &h.pipeline_efficiency},
                {"tileOverheadCycles", &h.tile_overhead_cycles},
                {"pairTileOverheadCycles", &h.pair_tile_overhead_cycles},
@@ -229,7 +231,8 @@ int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t er
     // ceiling are refused rather than loaded.
     if (h.num_sms <= 0 || h.clock_hz <= 0 || h.umma_cycles_128x256 <= 0 ||
         h.umma_m64_ratio <= 0 || h.smem_bytes_per_cycle <= 0 || h.l2_bytes_per_sec <= 0 ||
-        h.hbm_bytes_per_sec <= 0 || h.tma_box_cycles <= 0 || h.tma_box2_ratio <= 0 || h.pipeline_efficiency <= 0 || h.pipeline_efficiency > 1 ||
+        h.hbm_bytes_per_sec <= 0 || h.tma_box_cycles <= 0 || h.tma_box2_ratio <= 0 ||
+        h.tma_box32_ratio <= 0 || h.pipeline_efficiency <= 0 || h.pipeline_efficiency > 1 ||
         h.tile_overhead_cycles < 0 || h.pair_tile_overhead_cycles < 0 || h.c_write_bytes_per_sec <= 0 ||
         h.epi_bytes_per_cycle_w4 <= 0 ||
         h.epi_bytes_per_cycle_w8 <= 0 || h.tma_latency_cycles < 0 || h.launch_overhead_sec < 0 ||

@@ -179,7 +179,9 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     // thread, and stages alternate between two such thread pairs. An issuing
     // thread finishes about one box per tma_box_cycles whatever the box size
     // (measured), so a CTA fills one stage per tma_box_cycles / 2.
-    const double t_fill = hw->tma_box_cycles * (t.BK == 128 ? hw->tma_box2_ratio : 1.0) / 2.0;
+    const double box_ratio =
+        t.BK == 128 ? hw->tma_box2_ratio : (t.BK == 32 ? hw->tma_box32_ratio : 1.0);
+    const double t_fill = hw->tma_box_cycles * box_ratio / 2.0;
     const double stage_bytes = (double(g.rows_per_cta) + double(t.BN) / g.cg) * t.BK * 2.0;
     (void)stage_bytes;
     const double t_smem = mma_per_stage * t_read;

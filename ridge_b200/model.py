@@ -23,7 +23,7 @@ HW_KEYS = {  # JSON key -> struct field
     "ummaM64Ratio": "umma_m64_ratio", "smemBytesPerCycle": "smem_bytes_per_cycle",
     "smemMmaOverlap": "smem_mma_overlap", "l2BytesPerSec": "l2_bytes_per_sec",
     "hbmBytesPerSec": "hbm_bytes_per_sec", "tmaBoxCycles": "tma_box_cycles",
-    "tmaBoxCycles128Ratio": "tma_box2_ratio",
+    "tmaBoxCycles128Ratio": "tma_box2_ratio", "tmaBoxCycles32Ratio": "tma_box32_ratio",
     "pipelineEfficiency": "pipeline_efficiency",
     "tileOverheadCycles": "tile_overhead_cycles",
     "pairTileOverheadCycles": "pair_tile_overhead_cycles",
