@@ -13,11 +13,13 @@ with the microbenchmarks built into libridge_b200.so
                      memory, from the MMA cycle count at small N
   smemMmaOverlap     1 when those reads overlap the MMA (cycles = max), 0 when
                      they add (cycles = sum); whichever fits the N sweep better
-  l2BytesPerSec      aggregate TMA fill rate from an L2-resident tensor
+  l2BytesPerSec      TMA fill cap from an L2-resident tensor (best bytes per SM
+                     cycle of several issuer / box / residency mixes, at clockHz)
   hbmBytesPerSec     aggregate TMA fill rate from a tensor 8x larger than L2
   epiBytesPerCycleW4/W8  epilogue drain rate per SM with 4 / 8 warps (C in L2)
   cWriteBytesPerSec  aggregate rate the epilogue writes a C far larger than L2
-  tmaBytesPerCycle   per-SM TMA fill with the GEMM's four issuing threads
+  tmaBoxCycles       cycles (at the loaded clock) one issuing thread needs per box;
+                     tmaBoxCycles32Ratio / tmaBoxCycles128Ratio: BK=32 / BK=128 boxes
   tmaLatencyCycles   load latency: bytes in flight / per-SM rate at depth 1
   launchOverheadSec  back-to-back launch cost of an empty kernel
   clockHz            SM clock measured under full tensor load
@@ -277,28 +279,44 @@ def calibrate(verbose=True):
         t4, t8, tt4 / 1e12, tt8 / 1e12))
     raw["memset_bytes_per_sec"] = write_bw()
     log("memset %.2f TB/s" % (raw["memset_bytes_per_sec"] / 1e12))
-    # the per-SM TMA fill with the GEMM's four issuing lanes; eight for headroom
-    per_sm4, tot4 = tma(32 << 20, 128, 2, 1, 0, 4)
-    per_sm8, tot8 = tma(32 << 20, 128, 1, 1, 0, 8)
-    res["tmaBytesPerCycle"] = per_sm4
-    # BK=32 tiles load 64-byte-wide boxes (64B swizzle)
-    per_sm32, _ = tma(32 << 20, 128, 2, 1, 0, 4, 32)
-    res["tmaBoxCycles32Ratio"] = per_sm4 / (2.0 * per_sm32)
-    per_sm128, _ = tma(32 << 20, 128, 1, 1, 0, 4, 128)
-    res["tmaBoxCycles128Ratio"] = 2.0 * per_sm4 / per_sm128
-    log("tma fill, 4 issuers, two-atom boxes: %.1f B/cycle/SM -> box time ratio %.2f" % (
-        per_sm128, res["tmaBoxCycles128Ratio"]))
-    log("tma fill, 4 issuers, 64-byte boxes: %.1f B/cycle/SM -> box time ratio %.2f" % (
-        per_sm32, res["tmaBoxCycles32Ratio"]))
-    raw["tma_l2_box128_d1_issuers8"] = [per_sm8, tot8]
-    log("tma fill, 4 issuers %.1f B/cycle/SM, 8 issuers %.1f" % (per_sm4, per_sm8))
+    # Per-box cost with ONE issuing thread (below the L2 cap): cycles per
+    # box at the GEMM's loaded clock (the microbenchmark runs faster; its own
+    # clock is total / (SMs x per-SM rate)), and the cost of 64-byte (BK=32)
+    # and two-atom (BK=128) boxes relative to one-atom 128-byte boxes.
+    box1 = {}
+    for cols in (32, 64, 128):
+        ps, tot = tma(32 << 20, 128, 2, 1, 0, 1, cols)
+        box1[cols] = (ps, tot)
+        raw["tma_l2_box128x%d_d2_issuers1" % cols] = [ps, tot]
+    ps64, tot64 = box1[64]
+    micro_hz = tot64 / (148 * ps64)
+    res["tmaBoxCycles"] = 128 * 128 / ps64 * res["clockHz"] / micro_hz
+    res["tmaBoxCycles32Ratio"] = ps64 / (2.0 * box1[32][0])
+    res["tmaBoxCycles128Ratio"] = 2.0 * ps64 / box1[128][0]
+    log("tma box, 1 issuer: %.0f cycles at the loaded clock; 64-byte box x%.2f, two-atom box x%.2f"
+        % (res["tmaBoxCycles"], res["tmaBoxCycles32Ratio"], res["tmaBoxCycles128Ratio"]))
+    # The L2 -> shared memory cap: several issuers (the GEMM's four lanes; two
+    # CTAs per SM; 2-D and two-atom boxes) all level off near the same bytes per
+    # SM cycle, at whatever clock the run holds, so it is kept per cycle and
+    # stated at the loaded clock.
+    cap_per_cycle = 0.0
+    for rows, depth, ctas, iss, cols in ((128, 2, 1, 4, 64), (256, 2, 1, 2, 64),
+                                         (256, 1, 1, 4, 64), (128, 1, 2, 4, 64),
+                                         (128, 2, 1, 2, 128), (128, 1, 1, 8, 64)):
+        ps, tot = tma(32 << 20, rows, depth, ctas, 0, iss, cols)
+        raw["tma_l2_box%dx%d_d%d_c%d_issuers%d" % (rows, cols, depth, ctas, iss)] = [ps, tot]
+        cap_per_cycle = max(cap_per_cycle, ps)
+        log("tma L2 box %dx%d depth %d, %d CTA(s), %d issuers: %.1f B/cycle/SM  %.2f TB/s" % (
+            rows, cols, depth, ctas, iss, ps, tot / 1e12))
+    res["l2BytesPerSec"] = cap_per_cycle * 148 * res["clockHz"]
+    log("tma L2 fill cap %.1f B/cycle/SM = %.2f TB/s at the loaded clock" % (
+        cap_per_cycle, res["l2BytesPerSec"] / 1e12))
     raw["copy_bytes_per_sec"] = copy_bw()
     res["launchOverheadSec"] = launch_overhead()
     log("copy %.2f TB/s, launch %.2f us" % (raw["copy_bytes_per_sec"] / 1e12,
                                            res["launchOverheadSec"] * 1e6))
     res.update({"numSMs": 148, "l2Bytes": 126.0 * 1024 * 1024, "smemBytesPerSM": 233472,
                 "tmemColsPerSM": 512, "maxCtasPerSM": 32})
-    res["tmaBoxCycles"] = 4 * 128 * 128 / res.pop("tmaBytesPerCycle")
     res["pipelineEfficiency"] = 1.0
     res["tileOverheadCycles"] = 0.0
     res["pairTileOverheadCycles"] = 0.0

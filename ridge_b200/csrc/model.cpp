@@ -176,14 +176,17 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     const double t_one = ov * std::max(t_issue, t_read) + (1.0 - ov) * (t_issue + t_read);
     const double t_mma = mma_per_stage * t_one;
     // TMA fill: a stage is one box of A and one of B, each issued by its own
-    // thread, and stages alternate between two such thread pairs. An issuing
-    // thread finishes about one box per tma_box_cycles whatever the box size
-    // (measured), so a CTA fills one stage per tma_box_cycles / 2.
+    // thread, and stages alternate between two such thread pairs. Below the L2
+    // cap an issuing thread finishes about one box per tma_box_cycles whatever
+    // the box size (measured), so a CTA fills one stage per tma_box_cycles / 2;
+    // the stage's bytes also cannot arrive faster than this SM's share of the
+    // aggregate L2 -> shared memory rate.
     const double box_ratio =
         t.BK == 128 ? hw->tma_box2_ratio : (t.BK == 32 ? hw->tma_box32_ratio : 1.0);
-    const double t_fill = hw->tma_box_cycles * box_ratio / 2.0;
     const double stage_bytes = (double(g.rows_per_cta) + double(t.BN) / g.cg) * t.BK * 2.0;
-    (void)stage_bytes;
+    const double l2_bytes_per_cycle_sm = hw->l2_bytes_per_sec / hw->num_sms / hw->clock_hz;
+    const double t_fill =
+        soft_max(hw->tma_box_cycles * box_ratio / 2.0, stage_bytes / l2_bytes_per_cycle_sm);
     const double t_smem = mma_per_stage * t_read;
 
     // ---- residency and the persistent walk (with the launcher's split-K tail)

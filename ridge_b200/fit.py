@@ -6,7 +6,8 @@ them carry an effective value that no isolated benchmark shows. This step
 measures every registered variant on a CALIBRATION shape set that is disjoint
 from the registered validation sweep (data/sweep/b200-calibration.csv), then
 adjusts those constants, each within a bounded band around its microbenchmark
-value, to minimise the mean |log(predicted / measured)| over that set. Each
+value, to minimise the mean |log(predicted / measured)| over that set without
+raising the top-10 autotune regret on it. Each
 configuration can be weighted by (its throughput / its shape's best) ** p
 (--weight-power; default 0, unweighted) so that the top of the ranking, where
 the autotuner picks, counts more. The
@@ -52,6 +53,7 @@ FIT_BANDS = {
 # the microbenchmark value of a fitted constant is kept under this key prefix
 MICRO = "microbenchmark_"
 WEIGHT_POWER = 0.0
+GUARD_K = 10
 ABS_BANDS = {"tileOverheadCycles": (0.0, 4000.0), "pairTileOverheadCycles": (0.0, 4000.0)}
 
 
@@ -88,9 +90,28 @@ def _objective(rows, hw, weights):
     return tot / max(wsum, 1e-30)
 
 
+def _topk_regret(rows, hw, k=GUARD_K):
+    """Mean top-k autotune regret (fraction) over the shapes in `rows`."""
+    from .model import predict
+    by = {}
+    for r in rows:
+        p = predict(r["M"], r["N"], r["K"], r["config"], hw)["predicted_tflops"]
+        by.setdefault((r["M"], r["N"], r["K"]), []).append((p, r["tflops"]))
+    tot = 0.0
+    for rs in by.values():
+        best = max(m for _, m in rs)
+        picked = max(m for _, m in sorted(rs, key=lambda x: -x[0])[:k])
+        tot += (best - picked) / best if best > 0 else 0.0
+    return tot / max(len(by), 1)
+
+
 def fit(rows, base: dict, passes=4, steps=9, weight_power=WEIGHT_POWER, log=print):
     """Coordinate descent over FIT_BANDS / ABS_BANDS, each constant on a
-    geometric (or linear, for ABS_BANDS) grid that narrows every pass."""
+    geometric (or linear, for ABS_BANDS) grid that narrows every pass. A move
+    is taken only if it lowers the error without raising the top-GUARD_K
+    autotune regret on the same calibration shapes: the constants exist to
+    rank configurations, so a better average error bought with a worse ranking
+    is refused."""
     weights = _weights(rows, weight_power)
     tmp = Path("/tmp") / ("ridge_fit_%d.json" % id(rows))
     start = {k: float(base[k]) for k in list(FIT_BANDS) + list(ABS_BANDS)}
@@ -99,8 +120,10 @@ def fit(rows, base: dict, passes=4, steps=9, weight_power=WEIGHT_POWER, log=prin
     lo.update({k: ABS_BANDS[k][0] for k in ABS_BANDS})
     hi.update({k: ABS_BANDS[k][1] for k in ABS_BANDS})
     cur = dict(start)
-    best = _objective(rows, _hw_with(base, cur, tmp), weights)
-    log("fit: start mean |log error| %.4f" % best)
+    hw0 = _hw_with(base, cur, tmp)
+    best = _objective(rows, hw0, weights)
+    guard = _topk_regret(rows, hw0)
+    log("fit: start mean |log error| %.4f, top-%d regret %.2f%%" % (best, GUARD_K, 100 * guard))
     width = {k: 1.0 for k in cur}  # fraction of the band searched around the current value
     for ps in range(passes):
         for k in cur:
@@ -115,11 +138,15 @@ def fit(rows, base: dict, passes=4, steps=9, weight_power=WEIGHT_POWER, log=prin
             for v in cands:
                 trial = dict(cur)
                 trial[k] = v
-                obj = _objective(rows, _hw_with(base, trial, tmp), weights)
+                hw = _hw_with(base, trial, tmp)
+                obj = _objective(rows, hw, weights)
                 if obj < best - 1e-6:
-                    best, cur = obj, trial
+                    rg = _topk_regret(rows, hw)
+                    if rg <= guard + 1e-12:
+                        best, cur, guard = obj, trial, rg
             width[k] *= 0.5
-        log("fit: pass %d mean |log error| %.4f" % (ps + 1, best))
+        log("fit: pass %d mean |log error| %.4f, top-%d regret %.2f%%" % (
+            ps + 1, best, GUARD_K, 100 * guard))
     tmp.unlink(missing_ok=True)
     return cur, best
 
