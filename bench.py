@@ -40,7 +40,7 @@ N_SLAB = 4096
 METRIC = "FP16 GEMM TFLOP/s (4096^3) vs B200 peak"
 UNIT = "TFLOP/s"
 # Best 4096^3 config from the autotuner on B200 (model-pruned, top-k measured).
-BEST_CONFIG = dict(BM=256, BN=256, BK=64, stages=3, warps=4, groupM=8, cta_group=1)
+BEST_CONFIG = dict(BM=256, BN=256, BK=64, stages=5, warps=4, groupM=8, cta_group=2)
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -218,6 +218,8 @@ def run_ridge(args):
         dist.init_process_group("nccl", device_id=dev)
 
     cfg = rb.TileConfig(**BEST_CONFIG)
+    if args.config:
+        cfg = rb.TileConfig(*[int(x) for x in args.config.split(",")])
     # Inputs: one LCG stream from seed 0: A, then the full B (N x K storage);
     # each rank keeps its N-slab (rows [rank*N_SLAB, (rank+1)*N_SLAB) of B).
     a = torch.empty((M, K), dtype=torch.float16, device=dev)
@@ -361,6 +363,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ridge", "reference"], default="ridge")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default=None,
+                    help="BM,BN,BK,stages,warps,groupM,cta_group instead of the default tile")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
