@@ -206,6 +206,8 @@ def run_reference(args):
 
 
 def run_ridge(args):
+    import ctypes as C
+
     import torch
     import torch.distributed as dist
 
@@ -278,19 +280,23 @@ def run_ridge(args):
         raise RuntimeError("device error during the timed region")
 
     # ------------------------------------------------ end to end (host buffers)
+    # The user-facing host-buffer call, ridge_gemm_host: page-locked A and B in,
+    # C out, the copies pipelined against the kernel by M-panels inside the call.
     a_h = torch.empty((M, K), dtype=torch.float16).pin_memory()
     b_h = torch.empty((N_SLAB, K), dtype=torch.float16).pin_memory()
     c_h = torch.empty((M, N_SLAB), dtype=torch.float16).pin_memory()
     a_h.copy_(a)
     b_h.copy_(b)
-    a2 = torch.empty_like(a)
-    b2 = torch.empty_like(b)
-    c2 = torch.empty_like(c)
+    cc = cfg.to_c()
+
+    def host_call():
+        s = rb.lib.ridge_gemm_host(C.byref(cc), a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(),
+                                   M, N_SLAB, K, K, K, N_SLAB, args.panels, sh)
+        if s != 0:
+            raise rb.RidgeError(s, "ridge_gemm_host")
+
     for _ in range(max(1, args.warmup)):
-        a2.copy_(a_h, non_blocking=True)
-        b2.copy_(b_h, non_blocking=True)
-        launch(a2, b2, c2)
-        c_h.copy_(c2, non_blocking=True)
+        host_call()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -298,10 +304,7 @@ def run_ridge(args):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        a2.copy_(a_h, non_blocking=True)
-        b2.copy_(b_h, non_blocking=True)
-        launch(a2, b2, c2)
-        c_h.copy_(c2, non_blocking=True)
+        host_call()
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -310,7 +313,10 @@ def run_ridge(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = world * flops_step * args.steps / (e2e_ms * 1e-3) / 1e12
-    ok = bool(torch.equal(c2, c))
+    # Same kernel, but panels change the split-K tail plan (summation order):
+    # agreement to FP16 rounding, not bit for bit.
+    cr = c.float().cpu()
+    ok = bool(((c_h.float() - cr).norm() / cr.norm()).item() <= 1e-3)
 
     # ------------------------------------------------ report (rank 0)
     if rank == 0:
@@ -363,6 +369,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ridge", "reference"], default="ridge")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--panels", type=int, default=0,
+                    help="M-panels of the end-to-end host-buffer call (0 = its default)")
     ap.add_argument("--config", default=None,
                     help="BM,BN,BK,stages,warps,groupM,cta_group instead of the default tile")
     args = ap.parse_args(argv)

@@ -160,6 +160,26 @@ int ridge_gemm_launch_noalloc(const ridge_tile_config* cfg, const void* A, const
  * the reference. */
 int64_t ridge_gemm_noalloc_scratch_bytes(void);
 
+/*
+ * End-to-end GEMM on HOST buffers: C = A * B^T with A (M x lda), B (N x ldb),
+ * C (M x ldc) all FP16 in host memory; pitches need not be multiples of 8.
+ * Replaces the host-side sequence of the reference's harness (copy A and B in,
+ * KernelVariant::launch, copy C out: bench/measure.cu:121-150 and
+ * check-gemm.cu:206-246) with one call that pipelines the copies against the
+ * kernel: M is cut into `panels` row panels (0 = about 4), B and then each A
+ * panel go over on an internal copy stream, each panel's launch runs on
+ * `stream` as soon as its A panel has landed, and each finished C panel comes
+ * back on a second internal stream while later panels are still arriving.
+ * Returns after enqueueing; `stream` is ordered after the last C copy, so a
+ * stream synchronise makes C valid. Page-locked host buffers give the overlap
+ * (pageable ones work, serialised by the driver). Device staging buffers are
+ * kept per device and grown on demand; growing frees the old ones, which
+ * waits for the device. Calls on one device are ordered on the GPU.
+ */
+int ridge_gemm_host(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                    int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                    int32_t panels, void* stream);
+
 /* Same, addressing the variant by its table index. */
 int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,
                               int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,

@@ -106,6 +106,8 @@ SIGNATURES = {
     "ridge_gemm_launch_noalloc": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64,
                                             _i64, _i64, _i64, _i64, _vp]),
     "ridge_gemm_noalloc_scratch_bytes": (_i64, []),
+    "ridge_gemm_host": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                  _i64, _i64, C.c_int32, _vp]),
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                             _i64, _i64, _vp]),
     "ridge_device_error": (C.c_int, [C.c_int, C.POINTER(_i32)]),

@@ -142,6 +142,36 @@ def gemm(a, b, out=None, config: TileConfig | None = None, stream=None):
     return out
 
 
+def gemm_host(a, b, out=None, config: TileConfig | None = None, panels: int = 0, stream=None,
+              device=None):
+    """C = A @ B for HOST tensors (a (M, K), b (N, K), fp16, CPU; page-locked
+    for copy/compute overlap): ridge_gemm_host pipelines the copies in, the
+    kernel and the copy of C out by M-panels on `device` (default: torch's
+    current device). Asynchronous on `stream`: synchronise before reading out."""
+    import torch
+    if a.dtype != torch.float16 or b.dtype != torch.float16:
+        raise TypeError("ridge_b200.gemm_host takes float16 operands")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("expected a (M, K) and b (N, K), got %s and %s" % (tuple(a.shape),
+                                                                         tuple(b.shape)))
+    if a.is_cuda or b.is_cuda or (out is not None and out.is_cuda):
+        raise ValueError("ridge_b200.gemm_host takes host (CPU) tensors; use gemm on CUDA ones")
+    M, K = a.shape
+    N = b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, pin_memory=a.is_pinned())
+    if a.stride(1) != 1 or b.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("inner dimensions must be contiguous")
+    cfg = config or DEFAULT_CONFIG
+    c = cfg.to_c()
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        st = lib.ridge_gemm_host(C.byref(c), a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
+                                 max(a.stride(0), K, 1), max(b.stride(0), K, 1),
+                                 max(out.stride(0), N, 1), panels, _stream_handle(stream))
+    check(st, "ridge_gemm_host %dx%dx%d %s" % (M, N, K, cfg.tag()))
+    return out
+
+
 def device_error(clear: bool = True) -> int:
     """Synchronises the current device and returns its kernel error word
     (0 = no bounded wait expired)."""
