@@ -29,6 +29,7 @@ extern "C" {
 #define RIDGE_EIO (-4)      /* file missing or unparseable */
 #define RIDGE_ERANGE (-5)   /* index out of range */
 #define RIDGE_ENOSCRATCH (-6) /* launch needs more scratch than ridge_gemm_launch_noalloc has */
+#define RIDGE_ECOMM (-7)      /* NCCL missing or an NCCL call failed (ridge_gemm_sharded) */
 
 /* Human-readable text for any status returned by this library. */
 const char* ridge_status_string(int status);
@@ -362,8 +363,7 @@ int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, 
  * split by N-column slabs of B with A replicated: B_slab points at rows
  * [n0, n0 + n_slab) of the N x K storage of B, C_slab is M x n_slab row-major
  * (ldc). The slab bounds come from ridge_slab_bounds. Purely local: no
- * collective. The optional all-gather of C lives on the host side
- * (torch.distributed / NCCL), see ridge_b200.sharded.
+ * collective; ridge_gemm_sharded below adds the optional all-gather.
  */
 int ridge_slab_bounds(int64_t N, int32_t nranks, int32_t rank, int64_t align, int64_t* n0,
                       int64_t* n_slab);
@@ -378,6 +378,27 @@ int ridge_slab_bounds(int64_t N, int32_t nranks, int32_t rank, int64_t align, in
  */
 int ridge_slabs_to_rowmajor(const void* slabs, void* C, int64_t M, int64_t N, int32_t nranks,
                             int64_t slab_cols, int64_t ldc, void* stream);
+
+/*
+ * One rank's part of the N-slab GEMM, with the optional gather of the full C
+ * (no counterpart in the single-GPU reference; the C-ABI shape named for the
+ * sharded configuration). A (M x lda) is replicated; B_slab is this rank's
+ * rows [n0, n0 + n_slab) of B's N x K storage (ldb), n0 / n_slab from
+ * ridge_slab_bounds(N, nranks, rank, 256). C_slab receives this rank's slab
+ * as M x slab_cols row-major, slab_cols = ridge_slab_bounds' width for rank 0
+ * (columns past n_slab are scratch). With gather_full_c != 0, the slabs of
+ * all ranks are all-gathered over `nccl_comm` (an ncclComm_t of nranks ranks,
+ * this rank = `rank`) into `slabs` (nranks x M x slab_cols FP16) and re-laid
+ * out into C_full (M x N, ldc_full) on every rank (one rank: C_slab is
+ * copied to C_full, no communicator needed). Everything is enqueued on
+ * `stream`. NCCL is resolved at run time from the libnccl.so.2 already loaded
+ * in the process (else loaded); RIDGE_ECOMM if it is absent or the collective
+ * fails. Buffers are the caller's.
+ */
+int ridge_gemm_sharded(const ridge_tile_config* cfg, const void* A, const void* B_slab,
+                       void* C_slab, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                       int32_t nranks, int32_t rank, int32_t gather_full_c, void* nccl_comm,
+                       void* slabs, void* C_full, int64_t ldc_full, void* stream);
 
 #ifdef __cplusplus
 }

@@ -20,6 +20,7 @@ RIDGE_ENOTSUP = -3
 RIDGE_EIO = -4
 RIDGE_ERANGE = -5
 RIDGE_ENOSCRATCH = -6
+RIDGE_ECOMM = -7
 
 BOTTLENECKS = ["TENSOR_CORE", "SMEM", "HBM", "OCC", "WAVES", "ENVELOPE", "DOES_NOT_FIT",
                "EPILOGUE", "L2"]
@@ -106,6 +107,9 @@ SIGNATURES = {
     "ridge_gemm_launch_noalloc": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64,
                                             _i64, _i64, _i64, _i64, _vp]),
     "ridge_gemm_noalloc_scratch_bytes": (_i64, []),
+    "ridge_gemm_sharded": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
+                                     _i64, _i64, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp,
+                                     _i64, _vp]),
     "ridge_gemm_host": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                   _i64, _i64, C.c_int32, _vp]),
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,

@@ -94,7 +94,7 @@ def build(jobs: int | None = None, verbose: bool = False, ptxas_info: bool = Fal
     if tasks or not LIB.exists():
         tmp = LIB.with_suffix(".so.tmp")
         _run([NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs),
-              "-L", str(CUDA_HOME / "lib64"), "-lcudart", "-lpthread"], verbose)
+              "-L", str(CUDA_HOME / "lib64"), "-lcudart", "-lpthread", "-ldl"], verbose)
         os.replace(tmp, LIB)
     cli_src = CSRC / "ridge_predict_cli.cpp"
     if cli_src.exists() and (not CLI.exists() or CLI.stat().st_mtime < LIB.stat().st_mtime

@@ -473,6 +473,7 @@ const char* ridge_status_string(int s) {
         case RIDGE_ENOTSUP: return "not supported on this device (needs sm_100)";
         case RIDGE_EIO: return "file missing or unparseable";
         case RIDGE_ERANGE: return "index out of range";
+        case RIDGE_ECOMM: return "NCCL missing from the process or an NCCL call failed";
         case RIDGE_ENOSCRATCH:
             return "launch needs more split-K scratch than the fixed no-allocation array holds";
         default: break;

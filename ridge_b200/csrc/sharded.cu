@@ -10,9 +10,12 @@
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/ridge_b200.h"
 
@@ -58,6 +61,22 @@ __global__ void slabs_to_rowmajor_scalar(const uint16_t* __restrict__ slabs,
     }
 }
 
+// ncclAllGather from the process's libnccl.so.2: the one the caller's
+// communicator came from (a framework usually has it loaded already), so the
+// library does not link NCCL itself.
+using AllGatherFn = ncclResult_t (*)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                                     cudaStream_t);
+AllGatherFn nccl_allgather() {
+    static std::once_flag once;
+    static AllGatherFn fn = nullptr;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (h) fn = reinterpret_cast<AllGatherFn>(dlsym(h, "ncclAllGather"));
+    });
+    return fn;
+}
+
 }  // namespace
 
 extern "C" {
@@ -94,6 +113,39 @@ int ridge_slabs_to_rowmajor(const void* slabs, void* C, int64_t M, int64_t N, in
                                                         static_cast<uint16_t*>(C), M, N, nranks,
                                                         slab_cols, ldc);
     return int(cudaGetLastError());
+}
+
+int ridge_gemm_sharded(const ridge_tile_config* cfg, const void* A, const void* B_slab,
+                       void* C_slab, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                       int32_t nranks, int32_t rank, int32_t gather_full_c, void* nccl_comm,
+                       void* slabs, void* C_full, int64_t ldc_full, void* stream) {
+    constexpr int64_t kAlign = 256;
+    if (!cfg || M < 0 || N < 0 || K < 0) return RIDGE_EINVAL;
+    int64_t n0 = 0, ns = 0, per = 0, unused = 0;
+    int st = ridge_slab_bounds(N, nranks, rank, kAlign, &n0, &ns);
+    if (st != RIDGE_OK) return st;
+    st = ridge_slab_bounds(N, nranks, 0, kAlign, &unused, &per);
+    if (st != RIDGE_OK) return st;
+    if (gather_full_c && (!C_full || ldc_full < N || (nranks > 1 && (!nccl_comm || !slabs))))
+        return RIDGE_EINVAL;
+    if (M > 0 && ns > 0) {
+        st = ridge_gemm_launch(cfg, A, B_slab, C_slab, M, ns, K, lda, ldb, per, stream);
+        if (st != RIDGE_OK) return st;
+    }
+    if (!gather_full_c || M == 0 || N == 0) return RIDGE_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (nranks == 1) {
+        // nothing to exchange: the one slab is C
+        cudaError_t e = cudaMemcpy2DAsync(C_full, size_t(ldc_full) * 2, C_slab, size_t(per) * 2,
+                                          size_t(N) * 2, size_t(M), cudaMemcpyDeviceToDevice, s);
+        return int(e);
+    }
+    AllGatherFn ag = nccl_allgather();
+    if (!ag) return RIDGE_ECOMM;
+    if (ag(C_slab, slabs, size_t(M * per), ncclHalf, static_cast<ncclComm_t>(nccl_comm), s) !=
+        ncclSuccess)
+        return RIDGE_ECOMM;
+    return ridge_slabs_to_rowmajor(slabs, C_full, M, N, nranks, per, ldc_full, stream);
 }
 
 }  // extern "C"

@@ -24,6 +24,7 @@ import ctypes as C
 import json
 import os
 import sys
+from datetime import timedelta
 
 from ._native import check, lib
 from .gemm import TileConfig, _stream_handle, launch_raw
@@ -64,11 +65,22 @@ def slabs_to_rowmajor(slabs, C_out, M: int, N: int, nranks: int, slab_cols: int,
     return C_out
 
 
+def nccl_comm_ptr(group=None) -> int:
+    """The ncclComm_t behind a torch.distributed NCCL process group (default:
+    the world group), for ridge_gemm_sharded's gather."""
+    import torch
+    import torch.distributed as dist
+    pg = group if group is not None else dist.distributed_c10d._get_default_group()
+    return pg._get_backend(torch.device("cuda"))._comm_ptr()
+
+
 def sharded_gemm(a, b, config: TileConfig, gather: bool = False, group=None, rank=None,
-                 world=None):
-    """Rank-local part of the N-slab GEMM. `b` is either the full N x K
-    storage of B (this rank slices its rows) or already this rank's slab (then
-    pass the full N as b.full_n). Returns (c_slab, full_c or None)."""
+                 world=None, stream=None):
+    """Rank-local part of the N-slab GEMM through ridge_gemm_sharded. `b` is
+    either the full N x K storage of B (this rank slices its rows) or already
+    this rank's slab (then pass the full N as b.full_n). With gather=True the
+    slabs are all-gathered over the group's NCCL communicator and re-laid out
+    into the full row-major C on every rank. Returns (c_slab, full_c or None)."""
     import torch
     import torch.distributed as dist
     if world is None:
@@ -78,17 +90,27 @@ def sharded_gemm(a, b, config: TileConfig, gather: bool = False, group=None, ran
     N = getattr(b, "full_n", b.shape[0])
     n0, ns = slab_bounds(N, world, rank)
     b_slab = b if getattr(b, "full_n", None) is not None else b[n0:n0 + ns]
-    M = a.shape[0]
+    M, K = a.shape
     per = slab_width(N, world)
-    # The gather needs equal-size slabs: compute into a per-column-wide buffer.
+    # the gather needs equal-size slabs: compute into a slab-width buffer
     c_slab = torch.empty((M, max(per, 1)), dtype=torch.float16, device=a.device)
-    slab_gemm(a, b_slab, c_slab, config)
-    if not gather or world == 1:
-        return c_slab[:, :ns], (c_slab[:, :N] if world == 1 and gather else None)
-    slabs = torch.empty((world, M, per), dtype=torch.float16, device=a.device)
-    dist.all_gather_into_tensor(slabs.view(-1), c_slab.view(-1), group=group)
-    full = torch.empty((M, N), dtype=torch.float16, device=a.device)
-    slabs_to_rowmajor(slabs, full, M, N, world, per)
+    slabs = full = None
+    comm = None
+    if gather:
+        full = torch.empty((M, N), dtype=torch.float16, device=a.device)
+        if world > 1:
+            slabs = torch.empty((world, M, per), dtype=torch.float16, device=a.device)
+            comm = nccl_comm_ptr(group)
+    cc = config.to_c()
+    b_ptr = b_slab.data_ptr() if ns else a.data_ptr()   # unused when the slab is empty
+    st = lib.ridge_gemm_sharded(C.byref(cc), a.data_ptr(), b_ptr, c_slab.data_ptr(), M, N, K,
+                                max(a.stride(0), 1), max(b_slab.stride(0), 1) if ns else K,
+                                world, rank, 1 if gather else 0, comm,
+                                slabs.data_ptr() if slabs is not None else None,
+                                full.data_ptr() if full is not None else None,
+                                full.stride(0) if full is not None else N,
+                                _stream_handle(stream))
+    check(st, "ridge_gemm_sharded %dx%dx%d rank %d/%d" % (M, N, K, rank, world))
     return c_slab[:, :ns], full
 
 
@@ -106,6 +128,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--gather", action="store_true")
+    ap.add_argument("--timeout", type=float, default=120.0,
+                    help="seconds before a stuck collective is aborted")
     a = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -113,7 +137,9 @@ def main(argv=None):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        # a rank that never arrives ends the others' collectives with an error
+        # after the deadline instead of hanging them
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=a.timeout))
     cfg = TileConfig(*[int(x) for x in a.config.split(",")])
     M, N, K = (int(x) for x in a.shape.lower().split("x"))
     n0, ns = slab_bounds(N, world, rank)
@@ -143,28 +169,33 @@ def main(argv=None):
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    gather_ms = None
+    gather_ms = step_ms = None
     if a.gather and world > 1:
-        slabs = torch.empty((world, M, per), dtype=torch.float16, device=dev)
-        full = torch.empty((M, N), dtype=torch.float16, device=dev)
+        # the whole step through the C ABI: slab GEMM + NCCL all-gather + re-layout
+        B.full_n = N
+
+        def step():
+            sharded_gemm(A, B, cfg, gather=True, rank=rank, world=world)
+
         for _ in range(2):
-            dist.all_gather_into_tensor(slabs.view(-1), Cs.view(-1))
+            step()
         torch.cuda.synchronize()
         dist.barrier()
         e0.record()
         for _ in range(a.steps):
-            dist.all_gather_into_tensor(slabs.view(-1), Cs.view(-1))
-            slabs_to_rowmajor(slabs, full, M, N, world, per)
+            step()
         e1.record()
         torch.cuda.synchronize()
         g = torch.tensor([e0.elapsed_time(e1) / a.steps], dtype=torch.float64, device=dev)
         dist.all_reduce(g, op=dist.ReduceOp.MAX)
-        gather_ms = float(g.item())
+        step_ms = float(g.item())
+        gather_ms = step_ms - float(t.item())
     if rank == 0:
         tflops = 2.0 * M * N * K / (float(t.item()) * 1e-3) / 1e12
         print(json.dumps({"workload": "%dx%dx%d N-slab over %d GPU(s)" % (M, N, K, world),
                           "config": cfg.tag(), "ms_per_gemm_max_over_ranks": float(t.item()),
-                          "tflops_whole_node": tflops, "gather_ms": gather_ms}))
+                          "tflops_whole_node": tflops, "ms_gemm_plus_gather": step_ms,
+                          "gather_ms": gather_ms}))
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -130,3 +130,18 @@ def test_gpu_test_configs_are_valid():
     spec.loader.exec_module(mod)
     for c in mod.CONFIGS + [c for _, c in mod.SPLITK_CASES]:
         assert rb.config_ok(TileConfig(*c)), c
+
+
+def test_gemm_sharded_validates_before_touching_the_gpu():
+    """ridge_gemm_sharded refuses bad ranks and a gather without its buffers or
+    communicator up front (no launch, so this runs without a GPU)."""
+    import ctypes as C
+    from ridge_b200._native import RIDGE_EINVAL, lib
+    cfg = rb.TileConfig(128, 128, 64, 4, 4, 8).to_c()
+    args = lambda nranks, rank, gather, comm: (C.byref(cfg), None, None, None, 256, 1024, 64,
+                                                 64, 64, nranks, rank, gather, comm, None, None,
+                                                 1024, None)
+    assert lib.ridge_gemm_sharded(*args(2, 2, 0, None)) == RIDGE_EINVAL     # rank out of range
+    assert lib.ridge_gemm_sharded(*args(0, 0, 0, None)) == RIDGE_EINVAL     # no ranks
+    assert lib.ridge_gemm_sharded(*args(2, 0, 1, None)) == RIDGE_EINVAL     # gather, no comm
+    assert lib.ridge_status_string(-7).decode().startswith("NCCL")

@@ -1,0 +1,61 @@
+"""ridge_gemm_sharded on two real GPUs: each rank computes its N-slab, the
+slabs are all-gathered over the NCCL communicator torch.distributed created,
+and every rank ends with the full C, equal bit for bit to a one-GPU launch of
+the whole GEMM (split-K off, so each output tile is the same arithmetic).
+Skipped with fewer than two GPUs."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs two CUDA GPUs")]
+
+SHAPES = [(512, 1000, 384), (256, 4096, 1024)]
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import ridge_b200 as rb
+    from ridge_b200.sharded import sharded_gemm
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    try:
+        cfg = rb.TileConfig(128, 256, 64, 4, 4, 8, 0, 1)
+        for (M, N, K) in SHAPES:
+            a, b = rb.synthetic_inputs(M, N, K, device=dev)
+            c_slab, full = sharded_gemm(a, b, cfg, gather=True)
+            whole = rb.gemm(a, b, config=cfg)
+            torch.cuda.synchronize()
+            assert rb.device_error() == 0
+            assert torch.equal(full, whole), (rank, M, N, K)
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_sharded_gemm_gathers_the_whole_c():
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    results = dict(q.get(timeout=5) for _ in procs)
+    assert results == {0: "ok", 1: "ok"}, results
