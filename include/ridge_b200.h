@@ -234,6 +234,7 @@ typedef struct ridge_hw {
     double epi_bytes_per_cycle_w4;   /* [CAL] C bytes/cycle/SM drained by 4 epilogue warps */
     double epi_bytes_per_cycle_w8;   /* [CAL] same with 8 epilogue warps */
     double tma_latency_cycles;       /* [CAL] issue -> arrival latency of one stage load */
+    double tma_latency_hbm_cycles;   /* [CAL] the same when the operands stream from DRAM */
     double launch_overhead_sec;      /* [CAL] fixed cost of one launch (launch + fill + drain) */
     double l2_bytes;                 /* L2 capacity */
     int32_t smem_bytes_per_sm;

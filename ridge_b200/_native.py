@@ -50,7 +50,8 @@ class HwC(C.Structure):
                 ("tile_overhead_cycles", C.c_double), ("pair_tile_overhead_cycles", C.c_double),
                 ("c_write_bytes_per_sec", C.c_double),
                 ("epi_bytes_per_cycle_w4", C.c_double), ("epi_bytes_per_cycle_w8", C.c_double),
-                ("tma_latency_cycles", C.c_double), ("launch_overhead_sec", C.c_double),
+                ("tma_latency_cycles", C.c_double),
+                ("tma_latency_hbm_cycles", C.c_double), ("launch_overhead_sec", C.c_double),
                 ("l2_bytes", C.c_double), ("smem_bytes_per_sm", C.c_int32),
                 ("tmem_cols_per_sm", C.c_int32), ("max_ctas_per_sm", C.c_int32),
                 ("calibrated", C.c_int32)]

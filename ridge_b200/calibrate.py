@@ -21,6 +21,7 @@ with the microbenchmarks built into libridge_b200.so
   tmaBoxCycles       cycles (at the loaded clock) one issuing thread needs per box;
                      tmaBoxCycles32Ratio / tmaBoxCycles128Ratio: BK=32 / BK=128 boxes
   tmaLatencyCycles   load latency: bytes in flight / per-SM rate at depth 1
+  tmaLatencyHbmCycles  the same with the tensor in DRAM (8 GB, L2 misses)
   launchOverheadSec  back-to-back launch cost of an empty kernel
   clockHz            SM clock measured under full tensor load
 
@@ -260,6 +261,11 @@ def calibrate(verbose=True):
     raw["tma_l2_box128_depth_curve"] = curve
     res["tmaLatencyCycles"] = 128 * 128 / curve[1]
     log("tma latency (depth 1): %.0f cycles" % res["tmaLatencyCycles"])
+    # the same from a tensor far larger than L2: every box waits for DRAM
+    ps_hbm, _ = tma(8 << 30, 128, 1)
+    raw["tma_hbm_box128_d1"] = ps_hbm
+    res["tmaLatencyHbmCycles"] = 128 * 128 / ps_hbm
+    log("tma latency from DRAM (depth 1): %.0f cycles" % res["tmaLatencyHbmCycles"])
     res["epiBytesPerCycleW4"], _ = epi(4)
     res["epiBytesPerCycleW8"], _ = epi(8)
     log("epilogue (C in L2): %.1f / %.1f B/cycle/SM (4 / 8 warps)" % (

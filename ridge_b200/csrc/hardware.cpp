@@ -152,6 +152,7 @@ int ridge_hw_b200(ridge_hw* h) {
     h->epi_bytes_per_cycle_w4 = 32.0;
     h->epi_bytes_per_cycle_w8 = 48.0;
     h->tma_latency_cycles = 1000.0;
+    h->tma_latency_hbm_cycles = 1000.0;
     h->launch_overhead_sec = 4e-6;
     h->l2_bytes = 126.0 * 1024 * 1024;
     h->smem_bytes_per_sm = 233472;
@@ -204,6 +205,7 @@ int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t er
                {"epiBytesPerCycleW4", &h.epi_bytes_per_cycle_w4},
                {"epiBytesPerCycleW8", &h.epi_bytes_per_cycle_w8},
                {"tmaLatencyCycles", &h.tma_latency_cycles},
+               {"tmaLatencyHbmCycles", &h.tma_latency_hbm_cycles},
                {"launchOverheadSec", &h.launch_overhead_sec},
                {"l2Bytes", &h.l2_bytes}};
     for (const Req& r : dbl) {
@@ -235,7 +237,7 @@ int ridge_hw_load_json(const char* path, ridge_hw* out, char* errbuf, int32_t er
         h.tma_box32_ratio <= 0 || h.pipeline_efficiency <= 0 || h.pipeline_efficiency > 1 ||
         h.tile_overhead_cycles < 0 || h.pair_tile_overhead_cycles < 0 || h.c_write_bytes_per_sec <= 0 ||
         h.epi_bytes_per_cycle_w4 <= 0 ||
-        h.epi_bytes_per_cycle_w8 <= 0 || h.tma_latency_cycles < 0 || h.launch_overhead_sec < 0 ||
+        h.epi_bytes_per_cycle_w8 <= 0 || h.tma_latency_cycles < 0 || h.tma_latency_hbm_cycles < 0 || h.launch_overhead_sec < 0 ||
         h.l2_bytes <= 0 || h.smem_bytes_per_sm <= 0 || h.tmem_cols_per_sm <= 0 ||
         h.max_ctas_per_sm <= 0 || h.smem_mma_overlap < 0 || h.smem_mma_overlap > 1) {
         set_err(errbuf, errlen, std::string(path) + ": a required constant is out of range");

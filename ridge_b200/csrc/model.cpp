@@ -205,6 +205,17 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     const double resident =
         std::min(double(cps), std::max(1.0, double(grid_units) * g.cg / hw->num_sms));
 
+    // Operand bytes from DRAM (grouped-M walk, L2 reuse) against all operand
+    // bytes the TMA moves into shared memory: loads of panels no earlier round
+    // left in L2 wait for DRAM, not for L2.
+    const double a_b_reads =
+        dram_bytes(M, N, K, t.BM, t.BN, t.groupM, std::min(tiles, units), hw->l2_bytes) -
+        double(M) * N * 2.0;
+    const double fill_total = double(tiles) * kb * double(t.BM + t.BN) * t.BK * 2.0;
+    const double f_dram = std::min(1.0, std::max(0.0, a_b_reads / std::max(fill_total, 1.0)));
+    const double t_lat = hw->tma_latency_cycles +
+                         f_dram * std::max(0.0, hw->tma_latency_hbm_cycles - hw->tma_latency_cycles);
+
     // Shared on-SM resources (tensor core, shared memory) serve the resident
     // CTAs in turn; each CTA's fill and its load latency are its own.
     // The SM keeps about four boxes in flight in all (one CTA with four
@@ -214,8 +225,7 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     // A ring slot refills only after its MMAs finish: the load then waits
     // behind the pair's current box (t_fill) and travels for the unloaded
     // latency, so `stages` slots must cover (latency + t_fill + t_stage).
-    const double t_period = std::max(
-        t_stage, (hw->tma_latency_cycles + t_fill + t_stage) / double(t.stages));
+    const double t_period = std::max(t_stage, (t_lat + t_fill + t_stage) / double(t.stages));
     const double t_main_whole = kb * t_period;
 
     const double c_bytes_tile = double(g.rows_per_cta) * t.BN * 2.0;
@@ -246,14 +256,11 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     } else if (info.acc_buffers >= 2 && dp_per_unit > 0) {
         t_unit += std::min(t_main_whole, t_epi);  // the last tile's epilogue drains alone
     }
-    const double t_prologue = hw->tma_latency_cycles;
+    const double t_prologue = t_lat;
     t_unit += t_prologue;
     const double compute_sec = t_unit / hw->clock_hz + hw->launch_overhead_sec;
 
     // ---- HBM: operand reads (grouped-M walk, L2 reuse), C writes, split-K partials
-    const double a_b_reads =
-        dram_bytes(M, N, K, t.BM, t.BN, t.groupM, std::min(tiles, units), hw->l2_bytes) -
-        double(M) * N * 2.0;
     const double c_write = double(M) * N * 2.0;
     const double partial_traffic =
         splits >= 2 ? 2.0 * double(rem) * (splits - 1) * g.cg * double(g.rows_per_cta) * t.BN * 4.0

@@ -43,6 +43,7 @@ FIT_BANDS = {
     "tmaBoxCycles128Ratio": (0.5, 2.0),
     "tmaBoxCycles32Ratio": (0.5, 2.0),
     "tmaLatencyCycles": (0.5, 3.0),
+    "tmaLatencyHbmCycles": (0.5, 3.0),
     "pipelineEfficiency": (0.7, 1.0),
     "epiBytesPerCycleW4": (0.5, 2.0),
     "epiBytesPerCycleW8": (0.5, 2.0),

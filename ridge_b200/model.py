@@ -29,6 +29,7 @@ HW_KEYS = {  # JSON key -> struct field
     "pairTileOverheadCycles": "pair_tile_overhead_cycles",
     "cWriteBytesPerSec": "c_write_bytes_per_sec", "epiBytesPerCycleW4": "epi_bytes_per_cycle_w4",
     "epiBytesPerCycleW8": "epi_bytes_per_cycle_w8", "tmaLatencyCycles": "tma_latency_cycles",
+    "tmaLatencyHbmCycles": "tma_latency_hbm_cycles",
     "launchOverheadSec": "launch_overhead_sec", "l2Bytes": "l2_bytes",
     "smemBytesPerSM": "smem_bytes_per_sm", "tmemColsPerSM": "tmem_cols_per_sm",
     "maxCtasPerSM": "max_ctas_per_sm",
