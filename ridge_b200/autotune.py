@@ -20,6 +20,7 @@ for each k, pick the best measured config among the model's top k and report
 from __future__ import annotations
 
 import argparse
+import collections
 import csv
 import ctypes as C
 import statistics
@@ -80,8 +81,7 @@ def autotune(shapes, k=10, devices=(0,), hw: HwC | None = None, warmup=3, iters=
     return results, entries
 
 
-def write_csv(path, shapes, entries, hw: HwC, note=""):
-    from .gemm import config_info
+def write_header(path, hw: HwC, note=""):
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
     with open(path, "w", newline="") as f:
@@ -89,18 +89,94 @@ def write_csv(path, shapes, entries, hw: HwC, note=""):
         f.write("# hw_model,%s\n" % hw.name.decode())
         if note:
             f.write("# %s\n" % note)
+        csv.writer(f).writerow(CSV_FIELDS)
+
+
+def append_rows(path, shape, rows, hw: HwC):
+    from .gemm import config_info
+    M, N, K, tag = shape
+    with open(path, "a", newline="") as f:
         w = csv.writer(f)
-        w.writerow(CSV_FIELDS)
-        for shape, rows in zip(shapes, entries):
-            M, N, K, tag = shape
-            for r in rows:
-                c = r["config"]
-                info = config_info(c)
-                p = predict(M, N, K, c, hw)
-                w.writerow([M, N, K, tag, c.BM, c.BN, c.BK, c.stages, c.warps, c.groupM,
-                            info.config.cta_group, info.smem_bytes, info.threads, info.tmem_cols,
-                            "%.3f" % r["tflops"], "%.3f" % p["predicted_tflops"], p.label,
-                            r["device"]])
+        for r in rows:
+            c = r["config"]
+            info = config_info(c)
+            p = predict(M, N, K, c, hw)
+            w.writerow([M, N, K, tag, c.BM, c.BN, c.BK, c.stages, c.warps, c.groupM,
+                        info.config.cta_group, info.smem_bytes, info.threads, info.tmem_cols,
+                        "%.3f" % r["tflops"], "%.3f" % p["predicted_tflops"], p.label,
+                        r["device"]])
+
+
+def append_meta(path, key, value):
+    with open(path, "a") as f:
+        f.write("# %s,%s\n" % (key, value))
+
+
+def write_csv(path, shapes, entries, hw: HwC, note=""):
+    write_header(path, hw, note)
+    for shape, rows in zip(shapes, entries):
+        append_rows(path, shape, rows, hw)
+
+
+def completed_shapes(path):
+    """Shapes whose rows are all in an existing sweep file (resume)."""
+    from .gemm import num_variants
+    if not Path(path).exists():
+        return set()
+    counts = collections.Counter()
+    with open(path, newline="") as f:
+        for r in csv.DictReader(l for l in f if not l.startswith("#")):
+            counts[(int(r["M"]), int(r["N"]), int(r["K"]))] += 1
+    n = num_variants()
+    return {k for k, v in counts.items() if v >= n}
+
+
+CANARY = (4096, 4096, 4096)
+
+
+def canary_tflops(device=0):
+    """A fixed 4096^3 launch (the bench tile) timed on `device`: the drift check
+    of the reference's measure.cu, between shapes of a long sweep."""
+    import torch
+
+    from .gemm import DEFAULT_CONFIG, synthetic_inputs
+    M, N, K = CANARY
+    with torch.cuda.device(device):
+        a, b = synthetic_inputs(M, N, K, device=torch.device("cuda", device))
+        c = torch.empty((M, N), dtype=torch.float16, device=a.device)
+        ms = C.c_double()
+        cc = DEFAULT_CONFIG.to_c()
+        check(lib.ridge_time_gemm(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N,
+                                  K, K, K, N, 5, 20, torch.cuda.current_stream().cuda_stream,
+                                  C.byref(ms)), "canary")
+    return 2.0 * M * N * K / (ms.value * 1e-3) / 1e12
+
+
+def exhaustive(path, shapes, devices, hw: HwC, warmup=3, iters=10, resume=False, log=print):
+    """Every candidate of every shape, appended shape by shape (a killed sweep
+    resumes with resume=True), with a canary before the first and after every
+    shape; returns the canary drift fraction (max - min) / median."""
+    done = completed_shapes(path) if resume else set()
+    if not resume or not Path(path).exists():
+        write_header(path, hw, "devices %s" % list(devices))
+    canaries = [canary_tflops(devices[0])]
+    append_meta(path, "canary_tflops", "%.1f" % canaries[-1])
+    for shape in shapes:
+        if shape[:3] in done:
+            log("%6d x %6d x %6d  already measured, skipped" % shape[:3])
+            continue
+        t0 = time.time()
+        results, entries = autotune([shape], 0, devices, hw, warmup, iters)
+        append_rows(path, shape, entries[0], hw)
+        canaries.append(canary_tflops(devices[0]))
+        append_meta(path, "canary_tflops", "%.1f" % canaries[-1])
+        r = results[0]
+        log("%6d x %6d x %6d  best %8.1f TFLOP/s  %s  (%d candidates, %.1f s, canary %.0f)" % (
+            r["M"], r["N"], r["K"], r["best_tflops"], r["best"].tag(), r["candidates"],
+            time.time() - t0, canaries[-1]))
+    drift = (max(canaries) - min(canaries)) / statistics.median(canaries)
+    append_meta(path, "canary_drift_fraction", "%.4f" % drift)
+    return drift
 
 
 def load_measured(path):
@@ -166,6 +242,8 @@ def main(argv=None):
     ap.add_argument("--exhaustive", default=None, help="benchmark every candidate, write CSV")
     ap.add_argument("--regret", default=None, help="report regret against this measured CSV")
     ap.add_argument("--ks", default="1,3,5,10,20")
+    ap.add_argument("--resume", action="store_true",
+                    help="with --exhaustive: keep the shapes already complete in the file")
     a = ap.parse_args(argv)
     hw = load_hw(a.hw) if a.hw else default_hw()
     ks = [int(x) for x in a.ks.split(",")]
@@ -183,18 +261,20 @@ def main(argv=None):
         return 0
     shapes = load_sweep(a.sweep)
     devices = [int(x) for x in a.devices.split(",")]
+    if a.exhaustive:
+        drift = exhaustive(a.exhaustive, shapes, devices, hw, a.warmup, a.iters, a.resume)
+        print("canary drift %.1f%%%s" % (100 * drift, "  (above 5%: clocks moved during the "
+                                         "sweep, treat it with care)" if drift > 0.05 else ""))
+        print("wrote", a.exhaustive)
+        return 0
     t0 = time.time()
-    results, entries = autotune(shapes, 0 if a.exhaustive else a.k, devices, hw, a.warmup,
-                                a.iters)
+    results, entries = autotune(shapes, a.k, devices, hw, a.warmup, a.iters)
     dt = time.time() - t0
     for r in results:
         print("%6d x %6d x %6d  best %8.1f TFLOP/s  %s  (%d of %d benchmarked)" % (
             r["M"], r["N"], r["K"], r["best_tflops"], r["best"].tag(), r["benchmarked"],
             r["candidates"]))
     print("farm: %d devices, %.1f s" % (len(devices), dt))
-    if a.exhaustive:
-        write_csv(a.exhaustive, shapes, entries, hw, note="devices %s, %.1f s" % (devices, dt))
-        print("wrote", a.exhaustive)
     return 0
 
 

@@ -169,3 +169,23 @@ def test_cli_batch_keeps_rows_and_appends_predictions(tmp_path):
     p = predict(4096, 4096, 4096, rb.TileConfig(256, 256, 64, 3, 4, 8, 0), b200())
     assert float(row[9]) == pytest.approx(p["predicted_tflops"], rel=1e-5)
     assert len(lines) == 4
+
+
+def test_sweep_file_appends_and_resume(tmp_path):
+    """The exhaustive sweep appends shape by shape; a shape whose every variant
+    is in the file counts as done on resume, a partial one does not."""
+    from ridge_b200.autotune import append_meta, append_rows, completed_shapes, load_measured, \
+        write_header
+    from ridge_b200.model import default_hw
+    hw = default_hw()
+    p = tmp_path / "sweep.csv"
+    write_header(p, hw, "test")
+    table = [v.config for v in rb.variants()]
+    append_rows(p, (256, 256, 256, "a"), [{"config": c, "tflops": 1.0, "device": 0}
+                                          for c in table], hw)
+    append_rows(p, (512, 256, 256, "b"), [{"config": c, "tflops": 1.0, "device": 1}
+                                          for c in table[:5]], hw)
+    append_meta(p, "canary_tflops", "1400.0")
+    assert completed_shapes(p) == {(256, 256, 256)}
+    rows = load_measured(p)
+    assert len(rows) == len(table) + 5 and rows[-1]["device"] == "1"
