@@ -64,17 +64,64 @@ def _traffic(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clock and throttle reasons sampled DURING the timed region: an NVML
+    thread polling every millisecond between __enter__ and __exit__ (the timed
+    region is milliseconds long, too short for nvidia-smi's 100 ms loop), with
+    nvidia-smi as the fallback when NVML cannot be opened."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event-reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.nvml = None
+        self.samples = []      # (sm_mhz, reason bits)
+        self.max_mhz = None
+        self.lines = []
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        prop = torch.cuda.get_device_properties(self.index)
+        # the CUDA device as NVML sees it (CUDA_VISIBLE_DEVICES may renumber)
+        uuid = getattr(prop, "uuid", None)
+        if uuid is not None:
+            u = str(uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-")
+                                                             else "GPU-" + u)
+        if "CUDA_VISIBLE_DEVICES" in os.environ:
+            raise RuntimeError("cannot map the CUDA device to NVML")
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self):
+        nv, h = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(mhz), int(bits)))
+            except Exception:
+                break
+            time.sleep(0.001)
 
     def __enter__(self):
+        import threading
+        try:
+            self.nvml = self._nvml_handle()
+            nv, h = self.nvml
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._poll, daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
@@ -86,7 +133,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.nvml is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            return
         if self.proc is not None:
             time.sleep(0.2)
             self.proc.terminate()
@@ -98,25 +148,34 @@ class ClockSampler:
             self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
+        sm, mx, reasons = [], self.max_mhz, set()
+        if self.nvml is not None:
+            for mhz, bits in self.samples:
+                sm.append(mhz)
+                for name, bit in self.REASONS.items():
+                    if bits & bit:
+                        reasons.add(name)
+            source = "nvml 1 ms"
+        else:
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in self.lines:
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = float(f[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, f[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+            source = "nvidia-smi 100 ms"
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        busy = [s for s in sm if mx and s > 0.5 * mx] or sm
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"], "samples": 0}
+        busy = [x for x in sm if mx and x > 0.5 * mx] or sm
         return {"sm_mhz": statistics.median(busy), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": source}
 
 
 def _dist_env():
