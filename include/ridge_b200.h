@@ -157,6 +157,18 @@ int ridge_gemm_launch_noalloc(const ridge_tile_config* cfg, const void* A, const
                               void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                               int64_t ldc, void* stream);
 
+/*
+ * Self-test of the bounded device waits (no counterpart in the reference):
+ * launches one thread that waits, through the GEMM pipeline's own bounded
+ * mbarrier wait, on a barrier nothing completes, with a limit of limit_ns
+ * (1 ms .. 2 s) instead of the GEMM's 2 s. The wait expires, the kernel raises
+ * its abort flag, records code 6 in the device error word and returns; the
+ * context stays usable. *code receives the error word read back (6 expected),
+ * *waited_ns how long the wait ran. Clears the error word before and after.
+ * Synchronises the device. RIDGE_EDEVICE if the wait did not give up.
+ */
+int ridge_selftest_wait_timeout(int64_t limit_ns, int32_t* code, int64_t* waited_ns);
+
 /* Size in bytes of ridge_gemm_launch_noalloc's fixed per-device scratch. No counterpart in
  * the reference. */
 int64_t ridge_gemm_noalloc_scratch_bytes(void);

@@ -111,6 +111,7 @@ SIGNATURES = {
     "ridge_gemm_sharded": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
                                      _i64, _i64, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp,
                                      _i64, _vp]),
+    "ridge_selftest_wait_timeout": (C.c_int, [_i64, C.POINTER(C.c_int32), C.POINTER(_i64)]),
     "ridge_gemm_host": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                   _i64, _i64, C.c_int32, _vp]),
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,

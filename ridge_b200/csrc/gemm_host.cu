@@ -36,7 +36,29 @@ constexpr int kSmemPerSm = 233472;    // 228 KB per SM
 constexpr int kSmemReservedPerCta = 1024;
 constexpr int kTmemColsPerSm = 512;
 constexpr int64_t kCounterBytes = 64 * 1024;
-constexpr int64_t kMinSplitBlocks = 4;  // K-blocks per split-K range, at least  // split-K counter area at the head of a workspace
+constexpr int64_t kMinSplitBlocks = 4;  // K-blocks per split-K range, at least
+
+// The bounded-wait self-test: one thread waits on an mbarrier that nothing
+// will ever complete, through the same mbar_wait the GEMM's pipeline uses,
+// with a short limit; when it gives up it raises the abort flag and records
+// kErrSelfTest in the error word, exactly as a stalled GEMM stage would.
+__global__ void selftest_wait_kernel(int* err, uint64_t limit_ns, unsigned long long* waited,
+                                     int* abort_seen) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        mbar_init(smem_u32(&bar), 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = global_timer_ns();
+        const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_flag, err, kErrSelfTest, limit_ns);
+        *waited = global_timer_ns() - t0;
+        *abort_seen = ok ? -1 : abort_flag;
+    }
+}
 
 const std::vector<KernelEntry>& registry() {
     static const std::vector<KernelEntry> entries = [] {
@@ -565,6 +587,34 @@ int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, 
     const auto& t = variant_table();
     if (index < 0 || index >= int(t.size())) return RIDGE_ERANGE;
     return ridge_gemm_launch(&t[index], A, B, C, M, N, K, lda, ldb, ldc, stream);
+}
+
+int ridge_selftest_wait_timeout(int64_t limit_ns, int32_t* code, int64_t* waited_ns) {
+    if (limit_ns < 1000000 || limit_ns > 2000000000ll || !code || !waited_ns) return RIDGE_EINVAL;
+    int st = RIDGE_OK;
+    DeviceState* dev = device_state(&st);
+    if (!dev) return st;
+    // start from a clean error word so the code read back is this test's
+    int32_t before = 0;
+    if ((st = ridge_device_error(1, &before)) != RIDGE_OK) return st;
+    unsigned long long* d_waited = nullptr;
+    int* d_abort = nullptr;
+    cudaError_t e = cudaMalloc(&d_waited, sizeof(unsigned long long) + sizeof(int) * 2);
+    if (e != cudaSuccess) return int(e);
+    d_abort = reinterpret_cast<int*>(d_waited + 1);
+    selftest_wait_kernel<<<1, 32>>>(dev->err_word, uint64_t(limit_ns), d_waited, d_abort);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    unsigned long long w = 0;
+    int ab = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&w, d_waited, sizeof(w), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&ab, d_abort, sizeof(ab), cudaMemcpyDeviceToHost);
+    cudaFree(d_waited);
+    if (e != cudaSuccess) return int(e);
+    if ((st = ridge_device_error(1, code)) != RIDGE_OK) return st;
+    *waited_ns = int64_t(w);
+    // the wait must have given up (not completed) and raised the abort flag
+    return ab == 1 ? RIDGE_OK : RIDGE_EDEVICE;
 }
 
 int ridge_device_error(int clear, int32_t* code) {

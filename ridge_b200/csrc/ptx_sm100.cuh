@@ -23,6 +23,7 @@ enum DeviceErr : int {
     kErrTimeoutEpilogue = 3,   // epilogue waited too long for a finished accumulator
     kErrTimeoutDrain = 4,      // abort path: in-flight copies did not land in time
     kErrTimeoutSplitK = 5,     // split-K owner waited too long for another split's partial
+    kErrSelfTest = 6,          // ridge_selftest_wait_timeout: the wait expired as intended
 };
 
 // Wall-clock budget for any single mbarrier wait, in nanoseconds. A healthy
@@ -106,14 +107,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 // raises the CTA abort flag and records `code` in the device error word.
 template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          int* err, int code) {
+                                          int* err, int code,
+                                          uint64_t limit_ns = RIDGE_WAIT_LIMIT_NS) {
     if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
         if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 0) {
             if (abort != nullptr && *abort) return false;
-            if (global_timer_ns() - t0 > RIDGE_WAIT_LIMIT_NS) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 if (abort != nullptr) *abort = 1;
                 atomicCAS(err, 0, code);
                 return false;
