@@ -174,15 +174,16 @@ int default_cta_group(const ridge_tile_config& c) { return c.BM == 256 ? 2 : 1; 
 // stores: box = 32 columns (64 B, 64B swizzle) x box_rows rows. Stores that
 // fall outside rows/cols are clipped by the hardware.
 int make_output_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int64_t ld,
-                    int box_rows) {
+                    int box_rows, int box_cols) {
     auto enc = tensor_map_encoder();
     if (!enc) return RIDGE_ENOTSUP;
     cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
     cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
-    cuuint32_t box[2] = {32, cuuint32_t(box_rows)};
+    cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ptr, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? RIDGE_OK : RIDGE_EINVAL;
 }
@@ -456,7 +457,7 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     const bool tma_store = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && (ldc % 8) == 0;
     std::memset(&tmap_c, 0, sizeof(tmap_c));
     if (tma_store) {
-        st = make_output_map(&tmap_c, C, M, N, ldc, e->epi_rows);
+        st = make_output_map(&tmap_c, C, M, N, ldc, e->epi_rows, e->epi_cols);
         if (st != RIDGE_OK) return st;
     }
 

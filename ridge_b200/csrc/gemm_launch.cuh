@@ -44,6 +44,7 @@ KernelEntry make_entry() {
     e.tile_a_rows = T::kRowsA;
     e.tile_b_rows = T::kRowsB;
     e.epi_rows = T::kEpiRowsPerWarp;
+    e.epi_cols = T::kEpiBoxCols;
     e.partial_floats = T::kPartialFloats;
     e.stage_bytes = T::kStageBytes;
     e.fixed_smem = T::kAlignSlack + T::kEpiBytes + T::kBarrierBytes;

@@ -21,6 +21,7 @@ struct KernelEntry {
     int tile_a_rows;      // rows of A one CTA loads per stage (BM, or BM/2 for a 2-CTA pair)
     int tile_b_rows;      // rows of B (N x K storage) one CTA loads per stage
     int epi_rows;         // rows of one epilogue TMA store box
+    int epi_cols;         // columns of one epilogue TMA store box (32: 64B swizzle, 64: 128B)
     int partial_floats;   // FP32 floats of one CTA's split-K partial tile
     int stage_bytes;      // shared memory per pipeline stage, per CTA
     int fixed_smem;       // alignment slack + epilogue staging + barriers

@@ -86,9 +86,18 @@ struct GemmTraits {
                                      : kTmemColsRaw <= 256 ? 256
                                                            : 512;
     static constexpr int kThreads = (2 + kEpiWarps) * 32;
-    // Epilogue staging: per warp, two buffers of one 32-row x 32-column FP16
-    // chunk (rows of 64 B, 64B-swizzled) feeding TMA stores.
+    // Epilogue: each warp drains kEpiPerWarp chunks of 32 rows x 32 columns,
+    // kEpiLd at a time. With pairs, a pair of column-adjacent chunks goes out
+    // as one 32 x 64 TMA store from a 4 KB staging buffer (rows of 128 B,
+    // 128B-swizzled); otherwise each chunk is a 32 x 32 store from one of two
+    // 2 KB buffers (rows of 64 B, 64B-swizzled). 4 KB of staging per warp
+    // either way.
     static constexpr int kEpiRowsPerWarp = BM == 64 ? 16 : 32;
+    static constexpr int kEpiGroups = kEpiWarps / 4;  // warps sharing a TMEM lane quarter
+    static constexpr int kEpiPerHalf = (BN / 32) / kEpiGroups;
+    static constexpr int kEpiPerWarp = kMHalves * kEpiPerHalf;
+    static constexpr int kEpiLd = kEpiPerHalf % 2 == 0 ? 2 : 1;
+    static constexpr int kEpiBoxCols = 32 * kEpiLd;
     static constexpr int kEpiChunkBytes = 32 * 64;
     static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiChunkBytes;
     // FP32 floats of one CTA's split-K partial tile: 128 lanes x BN per M-half
@@ -395,7 +404,6 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         const int epi = warp - 2;
         const int quad = warp & 3;        // TMEM lane sub-partition this warp may access
         const int group = epi >> 2;       // column group when 8 warps share 4 sub-partitions
-        constexpr int kGroups = WARPS / 4;
         constexpr int kChunks = BN / 32;  // 32 FP32 columns per tcgen05.ld
         const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
         // Remote (leader) accumulator-empty barrier for the follower of a pair.
@@ -439,135 +447,206 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
             }
             __syncwarp();
-            // This warp's chunks of the tile, in order: M-half h, column chunk
-            // j = group, group + kGroups, ... The TMEM load of chunk ci + 1 is
-            // issued before chunk ci is stored, so its latency hides behind
+            // This warp's chunks of the tile are drained kLd at a time:
+            // both TMEM loads are issued before one wait (tcgen05.wait::ld
+            // waits for all of a thread's loads), and the next group's loads
+            // are issued before the current group is stored, so the TMEM load
+            // latency (hundreds of cycles while the tensor core is writing the
+            // other accumulator) is paid once per kLd chunks and hides behind
             // the stores.
-            constexpr int kPerHalf = kChunks / kGroups;
-            constexpr int kPerWarp = T::kMHalves * kPerHalf;
+            constexpr int kPerHalf = T::kEpiPerHalf;
+            constexpr int kPerWarp = T::kEpiPerWarp;
+            constexpr int kLd = T::kEpiLd;
+            // chunk ci of this warp: M-half ci / kPerHalf, column chunk
+            // group * kPerHalf + ci % kPerHalf (a warp's chunks are adjacent
+            // columns, so a pair forms one 64-column store)
             auto chunk_taddr = [&](int ci) {
-                const int hh = ci / kPerHalf, jj = group + (ci % kPerHalf) * kGroups;
+                const int hh = ci / kPerHalf, jj = group * kPerHalf + ci % kPerHalf;
                 return tmem_base + (uint32_t(quad * 32) << 16) +
                        uint32_t(acc * T::kAccCols + hh * BN + jj * 32);
             };
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(chunk_taddr(0), r);
-            tmem_wait_ld(r);
-#pragma unroll 1
-            for (int ci = 0; ci < kPerWarp; ++ci) {
-                const int h = ci / kPerHalf;
-                const int j = group + (ci % kPerHalf) * kGroups;
-                const bool more = ci + 1 < kPerWarp;
+            const int tile_row0 = tm * BM + int(rank) * T::kRowsA;
+            // Split-K partial chunks use a lane-contiguous layout: float4 v of
+            // lane L of chunk c sits at ((c * 8 + v) * 32 + L), so every
+            // warp-wide store or load covers 512 contiguous bytes. Producer
+            // and owner map warps to chunks identically.
+            auto ws_offset = [&](int ci) {
+                const int h = ci / kPerHalf, j = group * kPerHalf + ci % kPerHalf;
+                const long long chunk_id = (long long)(h * kChunks + j) * 4 + quad;
+                return chunk_id * 8 * 32 * 4 + lane * 4;
+            };
+            auto warp_row0_of = [&](int ci) {
                 // M=128 / 256-pair UMMA: row r of this CTA lives in TMEM lane r.
                 // M=64 UMMA: rows 16q..16q+15 live in lanes 32q..32q+15.
-                const int warp_row0 = BM == 64 ? quad * 16 : h * 128 + quad * 32;
-                const int tile_row0 = tm * BM + int(rank) * T::kRowsA;
+                return BM == 64 ? quad * 16 : (ci / kPerHalf) * 128 + quad * 32;
+            };
+            // A warp whose rows all lie at or beyond M has nothing to reduce.
+            auto warp_live_of = [&](int ci) {
+                return (long long)tile_row0 + warp_row0_of(ci) < p.M;
+            };
+            auto publish = [&](int ci, const uint32_t (&r)[32]) {
+                // Non-owner split: publish the FP32 partial chunk.
+                if (!warp_live_of(ci)) return;
+                float4* dst = reinterpret_cast<float4*>(
+                    ws_tile + (long long)(w.split - 1) * CG * kTileFloats + ws_offset(ci));
+#pragma unroll
+                for (int v = 0; v < 8; ++v)
+                    __stcg(dst + v * 32, make_float4(__uint_as_float(r[4 * v]),
+                                                     __uint_as_float(r[4 * v + 1]),
+                                                     __uint_as_float(r[4 * v + 2]),
+                                                     __uint_as_float(r[4 * v + 3])));
+            };
+            auto fold_and_pack = [&](int ci, uint32_t (&r)[32], uint32_t (&packed)[16]) {
+                if (w.split == 0 && warp_live_of(ci)) {
+                    // Owner: add the other splits' partials, in split order.
+                    for (int sp = 1; sp < p.sk_splits; ++sp) {
+                        const float4* src = reinterpret_cast<const float4*>(
+                            ws_tile + (long long)(sp - 1) * CG * kTileFloats + ws_offset(ci));
+                        float4 q[8];
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) q[v] = __ldcg(src + v * 32);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q[v].x);
+                            r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q[v].y);
+                            r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q[v].z);
+                            r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q[v].w);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+            };
+            auto store_chunk = [&](int ci, const uint32_t (&packed)[16]) {
+                const int j = group * kPerHalf + ci % kPerHalf;
+                const int warp_row0 = warp_row0_of(ci);
+                const int col0 = tn * BN + j * 32;
+                if (p.tma_store) {
+                    // Stage this warp's 32 x 32 chunk (one 64-byte row per
+                    // lane, 64B-swizzled: 16-byte unit c of row r sits at
+                    // unit c ^ ((r >> 1) & 3), conflict-free) and hand it to
+                    // a TMA store, which clips rows/columns outside C.
+                    // Buffer b's stores are issued (and waited on) by lane b,
+                    // so the warp has two issuing threads.
+                    const uint32_t sbuf = stage_buf0 + uint32_t(buf * T::kEpiChunkBytes);
+                    if (lane == buf) tma_store_wait_read<0>();  // this buffer's last store has read it
+                    __syncwarp();
+                    const uint32_t row_addr = sbuf + uint32_t(lane * 64);
+                    const uint32_t sw = uint32_t((lane >> 1) & 3);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                         row_addr + ((uint32_t(c) ^ sw) << 4)),
+                                     "r"(packed[4 * c]), "r"(packed[4 * c + 1]),
+                                     "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
+                                     : "memory");
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == buf) {
+                        tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0);
+                        tma_store_commit();
+                    }
+                    buf ^= 1;
+                    return;
+                }
                 const bool row_live = (BM != 64 || lane < 16);
                 const long long row = (long long)tile_row0 + warp_row0 + lane;
-                const bool row_ok = row_live && row < p.M;
-                // A warp whose rows all lie at or beyond M has nothing to reduce.
-                const bool warp_live = (long long)tile_row0 + warp_row0 < p.M;
-                {
-                    // Split-K partial chunks use a lane-contiguous layout: float4
-                    // v of lane L of chunk c sits at ((c * 8 + v) * 32 + L), so
-                    // every warp-wide store or load covers 512 contiguous bytes.
-                    // Producer and owner map warps to chunks identically.
-                    const long long chunk_id = (long long)(h * kChunks + j) * 4 + quad;
-                    const long long ws_off = chunk_id * 8 * 32 * 4 + lane * 4;
-                    if (w.split > 0) {
-                        // Non-owner split: publish the FP32 partial chunk.
-                        if (warp_live) {
-                            float4* dst = reinterpret_cast<float4*>(
-                                ws_tile + (long long)(w.split - 1) * CG * kTileFloats + ws_off);
+                if (!row_live || row >= p.M) return;
+                __half* crow = p.C + row * p.ldc;
+                if (vec_ok && col0 + 32 <= p.N) {
+                    uint4* dst = reinterpret_cast<uint4*>(crow + col0);
 #pragma unroll
-                            for (int v = 0; v < 8; ++v)
-                                __stcg(dst + v * 32, make_float4(__uint_as_float(r[4 * v]),
-                                                                 __uint_as_float(r[4 * v + 1]),
-                                                                 __uint_as_float(r[4 * v + 2]),
-                                                                 __uint_as_float(r[4 * v + 3])));
-                        }
-                        if (more) {
-                            __syncwarp();
-                            tmem_ld_32x32b_x32(chunk_taddr(ci + 1), r);
-                            tmem_wait_ld(r);
-                        }
-                        continue;  // warp-uniform: w.split is the same on every lane
+                    for (int v = 0; v < 4; ++v)
+                        dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
+                                            packed[4 * v + 3]);
+                } else {
+                    // Ragged columns: element stores, fully unrolled so
+                    // `packed` stays in registers.
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const uint32_t word = packed[e >> 1];
+                        const unsigned short bits = (e & 1) ? (unsigned short)(word >> 16)
+                                                            : (unsigned short)(word & 0xffff);
+                        if (col0 + e < p.N) crow[col0 + e] = __ushort_as_half(bits);
                     }
-                    if (w.split == 0 && warp_live) {
-                        // Owner: add the other splits' partials, in split order.
-                        for (int sp = 1; sp < p.sk_splits; ++sp) {
-                            const float4* src = reinterpret_cast<const float4*>(
-                                ws_tile + (long long)(sp - 1) * CG * kTileFloats + ws_off);
-                            float4 q[8];
+                }
+            };
+            // One 32 x 64 TMA store of chunks ci, ci + 1 (column-adjacent).
+            // Row r of the 4 KB buffer is 128 B; its 16-byte unit c sits at
+            // c ^ (r & 7) (the 128B swizzle, conflict-free).
+            auto store_pair = [&](int ci, const uint32_t (&pa)[16], const uint32_t (&pb)[16]) {
+                const int j = group * kPerHalf + ci % kPerHalf;
+                const int col0 = tn * BN + j * 32;
+                const uint32_t sbuf = stage_buf0;
+                // the previous pair's store (issued by lane 0) has read the buffer
+                if (lane == 0) tma_store_wait_read<0>();
+                __syncwarp();
+                const uint32_t row_addr = sbuf + uint32_t(lane * 128);
+                const uint32_t sw = uint32_t(lane & 7);
 #pragma unroll
-                            for (int v = 0; v < 8; ++v) q[v] = __ldcg(src + v * 32);
-#pragma unroll
-                            for (int v = 0; v < 8; ++v) {
-                                r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q[v].x);
-                                r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q[v].y);
-                                r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q[v].z);
-                                r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q[v].w);
-                            }
-                        }
-                    }
-                    uint32_t packed[16];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                for (int c = 0; c < 4; ++c) {
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                     row_addr + ((uint32_t(c) ^ sw) << 4)),
+                                 "r"(pa[4 * c]), "r"(pa[4 * c + 1]), "r"(pa[4 * c + 2]),
+                                 "r"(pa[4 * c + 3])
+                                 : "memory");
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                     row_addr + ((uint32_t(c + 4) ^ sw) << 4)),
+                                 "r"(pb[4 * c]), "r"(pb[4 * c + 1]), "r"(pb[4 * c + 2]),
+                                 "r"(pb[4 * c + 3])
+                                 : "memory");
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0_of(ci));
+                    tma_store_commit();
+                }
+            };
+            uint32_t ra[32], rb[32];
+            auto load_group = [&](int ci) {
+                tmem_ld_32x32b_x32(chunk_taddr(ci), ra);
+                if constexpr (kLd == 2) tmem_ld_32x32b_x32(chunk_taddr(ci + 1), rb);
+            };
+            auto wait_group = [&]() {
+                tmem_wait_ld(ra);
+                if constexpr (kLd == 2) tmem_wait_ld(rb);
+            };
+            load_group(0);
+            wait_group();
+#pragma unroll 1
+            for (int ci = 0; ci < kPerWarp; ci += kLd) {
+                const bool more = ci + kLd < kPerWarp;
+                if (w.split > 0) {
+                    publish(ci, ra);
+                    if constexpr (kLd == 2) publish(ci + 1, rb);
                     if (more) {
                         __syncwarp();
-                        tmem_ld_32x32b_x32(chunk_taddr(ci + 1), r);  // lands while we store
+                        load_group(ci + kLd);
+                        wait_group();
                     }
-                    const int col0 = tn * BN + j * 32;
-                    if (p.tma_store) {
-                        // Stage this warp's 32 x 32 chunk (one 64-byte row per
-                        // lane, 64B-swizzled: 16-byte unit c of row r sits at
-                        // unit c ^ ((r >> 1) & 3), conflict-free) and hand it to
-                        // a TMA store, which clips rows/columns outside C.
-                        // Buffer b's stores are issued (and waited on) by lane b,
-                        // so the warp has two issuing threads.
-                        const uint32_t sbuf = stage_buf0 + uint32_t(buf * T::kEpiChunkBytes);
-                        if (lane == buf) tma_store_wait_read<0>();  // this buffer's last store has read it
-                        __syncwarp();
-                        const uint32_t row_addr = sbuf + uint32_t(lane * 64);
-                        const uint32_t sw = uint32_t((lane >> 1) & 3);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                             row_addr + ((uint32_t(c) ^ sw) << 4)),
-                                         "r"(packed[4 * c]), "r"(packed[4 * c + 1]),
-                                         "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
-                                         : "memory");
-                        }
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == buf) {
-                            tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0);
-                            tma_store_commit();
-                        }
-                        buf ^= 1;
-                    } else if (row_ok) {
-                        __half* crow = p.C + row * p.ldc;
-                        if (vec_ok && col0 + 32 <= p.N) {
-                            uint4* dst = reinterpret_cast<uint4*>(crow + col0);
-#pragma unroll
-                            for (int v = 0; v < 4; ++v)
-                                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1],
-                                                    packed[4 * v + 2], packed[4 * v + 3]);
-                        } else {
-                            // Ragged columns: element stores, fully unrolled so
-                            // `packed` stays in registers.
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) {
-                                const uint32_t word = packed[e >> 1];
-                                const unsigned short bits = (e & 1) ? (unsigned short)(word >> 16)
-                                                                    : (unsigned short)(word & 0xffff);
-                                if (col0 + e < p.N) crow[col0 + e] = __ushort_as_half(bits);
-                            }
-                        }
-                    }
-                    if (more) tmem_wait_ld(r);
+                    continue;  // warp-uniform: w.split is the same on every lane
                 }
+                uint32_t pa[16], pb[16];
+                fold_and_pack(ci, ra, pa);
+                if constexpr (kLd == 2) fold_and_pack(ci + 1, rb, pb);
+                if (more) {
+                    __syncwarp();
+                    load_group(ci + kLd);  // lands while this group is stored
+                }
+                if constexpr (kLd == 2) {
+                    if (p.tma_store) {
+                        store_pair(ci, pa, pb);
+                    } else {
+                        store_chunk(ci, pa);
+                        store_chunk(ci + 1, pb);
+                    }
+                } else {
+                    store_chunk(ci, pa);
+                }
+                if (more) wait_group();
             }
             if (w.split > 0) {
                 // Make this warp's partial chunks visible, then count them.
@@ -591,7 +670,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 acc_phase ^= 1u;
             }
         }
-        if (p.tma_store && lane < 2) tma_store_wait_all<0>();
+        if (p.tma_store && lane < 2) tma_store_wait_all<0>();  // lanes 0 and 1 issue stores
     }
 
     tc_fence_before();
