@@ -276,6 +276,7 @@ struct LaunchPlan {
     const KernelEntry* e = nullptr;
     int idx = -1;
     int smem = 0;
+    int epi_stride = 4096;  // epilogue staging bytes per warp (8192: double-buffered pairs)
     int grid_units = 0;  // CTAs (1-CTA kernels) or CTA pairs
     int dp_tiles = 0, sk_tiles = 0, sk_splits = 1;
     size_t ws_partials = 0;  // bytes of FP32 partial tiles
@@ -338,6 +339,20 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     plan->e = e;
     plan->idx = idx;
     plan->smem = launch_smem(*e, cfg.stages);
+    // Kernels that store 32 x 64 pairs get a second 4 KB staging buffer per
+    // warp when it fits without costing a co-resident CTA: the next pair is
+    // then staged while the previous store is still reading the first.
+    plan->epi_stride = 4096;
+    if (e->epi_cols == 64) {
+        const int want = std::max(plan->smem, smem_for(*e, cfg.stages) + e->warps * 4096);
+        auto resident = [&](int s) {
+            return std::min(kSmemPerSm / (s + kSmemReservedPerCta), kTmemColsPerSm / e->tmem_cols);
+        };
+        if (want <= kMaxDynSmem && resident(want) == resident(plan->smem)) {
+            plan->smem = want;
+            plan->epi_stride = 8192;
+        }
+    }
     int st = ensure_smem_attr(*e, idx, dev);
     if (st != RIDGE_OK) return st;
     const int64_t tiles = ((M + e->BM - 1) / e->BM) * ((N + e->BN - 1) / e->BN);
@@ -470,6 +485,7 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     p.groupM = cfg->groupM;
     p.stages = cfg->stages;
     p.tma_store = tma_store ? 1 : 0;
+    p.epi_stride = plan.epi_stride;
     p.err = dev->err_word;
     p.dp_tiles = plan.dp_tiles;
     p.sk_tiles = plan.sk_tiles;

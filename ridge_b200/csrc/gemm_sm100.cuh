@@ -119,6 +119,7 @@ struct GemmParams {
     int groupM;
     int stages;
     int tma_store;  // 1: epilogue stores through the C tensor map; 0: direct st.global
+    int epi_stride; // staging bytes per epilogue warp: 4096, or 8192 for two pair buffers
     int* err;
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
     // one per unit per round; the remaining sk_tiles tiles are each split into
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
 
     const int stages = p.stages;
     const uint32_t epi_base = base + stages * T::kStageBytes;
-    const uint32_t bars = epi_base + T::kEpiBytes;
+    const uint32_t bars = epi_base + uint32_t(T::kEpiWarps * p.epi_stride);
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (kMaxStages + s); };
     auto tfull_bar = [&](int b) { return bars + 8u * (2 * kMaxStages + b); };
@@ -408,7 +409,9 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
         // Remote (leader) accumulator-empty barrier for the follower of a pair.
         const uint32_t tempty0 = CG == 2 ? map_to_cta(tempty_bar(0), 0) : tempty_bar(0);
-        const uint32_t stage_buf0 = epi_base + uint32_t(epi * 2 * T::kEpiChunkBytes);
+        const uint32_t stage_buf0 = epi_base + uint32_t(epi * p.epi_stride);
+        const bool two_pair_bufs = p.epi_stride >= 2 * 4096;
+        uint32_t pidx = 0;  // pair stores of this warp so far
         int buf = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -579,9 +582,15 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             auto store_pair = [&](int ci, const uint32_t (&pa)[16], const uint32_t (&pb)[16]) {
                 const int j = group * kPerHalf + ci % kPerHalf;
                 const int col0 = tn * BN + j * 32;
-                const uint32_t sbuf = stage_buf0;
-                // the previous pair's store (issued by lane 0) has read the buffer
-                if (lane == 0) tma_store_wait_read<0>();
+                // one buffer: the previous pair's store (issued by lane 0) has
+                // read it; two: the store before that one has read this one
+                const uint32_t sbuf = stage_buf0 + (two_pair_bufs ? (pidx & 1u) * 4096u : 0u);
+                if (lane == 0) {
+                    if (two_pair_bufs)
+                        tma_store_wait_read<1>();
+                    else
+                        tma_store_wait_read<0>();
+                }
                 __syncwarp();
                 const uint32_t row_addr = sbuf + uint32_t(lane * 128);
                 const uint32_t sw = uint32_t(lane & 7);
@@ -604,6 +613,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                     tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0_of(ci));
                     tma_store_commit();
                 }
+                ++pidx;
             };
             uint32_t ra[32], rb[32];
             auto load_group = [&](int ci) {
