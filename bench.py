@@ -40,7 +40,7 @@ N_SLAB = 4096
 METRIC = "FP16 GEMM TFLOP/s (4096^3) vs B200 peak"
 UNIT = "TFLOP/s"
 # Best 4096^3 config from the autotuner on B200 (model-pruned, top-k measured).
-BEST_CONFIG = dict(BM=256, BN=256, BK=64, stages=5, warps=4, groupM=8, cta_group=2)
+BEST_CONFIG = dict(BM=256, BN=256, BK=64, stages=6, warps=4, groupM=8, cta_group=2)
 L2_FLUSH_BYTES = 256 << 20
 
 

@@ -131,6 +131,38 @@ def completed_shapes(path):
     return {k for k, v in counts.items() if v >= n}
 
 
+def merge_best(out_path, in_paths):
+    """Per configuration the best throughput over several complete sweeps of the
+    same registered cross product (e.g. on separate boxes): single
+    configurations can move by tens of percent between sweeps while the median
+    barely moves, and those outliers decide top-k regret."""
+    key = ("M", "N", "K", "BM", "BN", "BK", "stages", "warps", "cta_group")
+    merged, order, meta = {}, [], []
+    fields = None
+    for i, path in enumerate(in_paths):
+        lines = Path(path).read_text().splitlines()
+        meta += ["# sweep %d %s" % (i + 1, l[2:]) for l in lines if l.startswith("# ")][1:]
+        rows = list(csv.DictReader(l for l in lines if not l.startswith("#")))
+        fields = fields or list(rows[0].keys())
+        for r in rows:
+            k = tuple(r[x] for x in key)
+            if k not in merged:
+                merged[k] = r
+                order.append(k)
+            elif float(r["tflops"]) > float(merged[k]["tflops"]):
+                merged[k] = r
+    with open(out_path, "w", newline="") as f:
+        f.write("# ridge B200 measured sweep (libridge_b200 ridge_autotune, exhaustive)\n")
+        f.write("# per configuration the best of %d complete sweeps (each best of 3 timed runs)\n"
+                % len(in_paths))
+        for m in meta:
+            f.write(m + "\n")
+        w = csv.DictWriter(f, fieldnames=fields)
+        w.writeheader()
+        w.writerows(merged[k] for k in order)
+    return len(order)
+
+
 CANARY = (4096, 4096, 4096)
 
 
@@ -244,7 +276,14 @@ def main(argv=None):
     ap.add_argument("--ks", default="1,3,5,10,20")
     ap.add_argument("--resume", action="store_true",
                     help="with --exhaustive: keep the shapes already complete in the file")
+    ap.add_argument("--merge", nargs="+", default=None, metavar="CSV",
+                    help="OUT IN1 IN2 ...: per configuration the best of several sweeps")
     a = ap.parse_args(argv)
+    if a.merge:
+        n = merge_best(a.merge[0], a.merge[1:])
+        print("merged %d configurations from %d sweeps into %s" % (n, len(a.merge) - 1,
+                                                                  a.merge[0]))
+        return 0
     hw = load_hw(a.hw) if a.hw else default_hw()
     ks = [int(x) for x in a.ks.split(",")]
     if a.regret:

@@ -229,14 +229,14 @@ int ctas_per_sm(const KernelEntry& e, int stages) {
 
 // The registered table: the full grid BM, BN in {64,128,256}, BK in {32,64}
 // (BASELINE) widened with BK=128 (two K atoms per TMA box, half the boxes per
-// unit of MMA work), stages in {2..5}, warps in {4,8}, groupM 8, minus the
+// unit of MMA work), stages in {2..6}, warps in {4,8}, groupM 8, minus the
 // points that overflow shared memory; BM=256 appears twice, as the 2-CTA pair
 // and as the single-CTA form.
 const std::vector<ridge_tile_config>& variant_table() {
     static const std::vector<ridge_tile_config> table = [] {
         std::vector<ridge_tile_config> t;
         const int bms[] = {64, 128, 256}, bns[] = {64, 128, 256}, bks[] = {32, 64, 128};
-        const int stages[] = {2, 3, 4, 5}, warps[] = {4, 8};
+        const int stages[] = {2, 3, 4, 5, 6}, warps[] = {4, 8};
         for (int bm : bms)
             for (int bn : bns)
                 for (int bk : bks)

@@ -189,3 +189,21 @@ def test_sweep_file_appends_and_resume(tmp_path):
     assert completed_shapes(p) == {(256, 256, 256)}
     rows = load_measured(p)
     assert len(rows) == len(table) + 5 and rows[-1]["device"] == "1"
+
+
+def test_merge_best_of_sweeps(tmp_path):
+    """Merging sweeps keeps, per configuration, the highest throughput."""
+    from ridge_b200.autotune import append_rows, load_measured, merge_best, write_header
+    from ridge_b200.model import default_hw
+    hw = default_hw()
+    table = [v.config for v in rb.variants()][:3]
+    paths = []
+    for i, vals in enumerate(([1.0, 5.0, 3.0], [2.0, 4.0, 6.0])):
+        p = tmp_path / ("s%d.csv" % i)
+        write_header(p, hw, "run %d" % i)
+        append_rows(p, (256, 256, 256, "a"), [{"config": c, "tflops": v, "device": i}
+                                              for c, v in zip(table, vals)], hw)
+        paths.append(p)
+    out = tmp_path / "m.csv"
+    assert merge_best(out, paths) == 3
+    assert [r["tflops"] for r in load_measured(out)] == [2.0, 5.0, 6.0]

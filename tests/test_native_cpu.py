@@ -38,7 +38,7 @@ def _smem_bytes(bm, bn, bk, s, w, cg):
 
 
 def test_variant_table_is_the_valid_grid():
-    """BM, BN in {64,128,256} x BK in {32,64} (widened with 128) x stages 2..5 x warps {4,8}, with
+    """BM, BN in {64,128,256} x BK in {32,64} (widened with 128) x stages 2..6 x warps {4,8}, with
     BM=256 both as a 2-CTA pair and as one CTA: every point whose shared memory
     fits in 227 KB is registered, every other point is refused. The four grid
     points whose operand ring alone overflows are among the refused."""
@@ -50,7 +50,7 @@ def test_variant_table_is_the_valid_grid():
     for bm in (64, 128, 256):
         for bn in (64, 128, 256):
             for bk in (32, 64, 128):
-                for s in (2, 3, 4, 5):
+                for s in (2, 3, 4, 5, 6):
                     for w in (4, 8):
                         for cg in ((1, 2) if bm == 256 else (1,)):
                             fits = _smem_bytes(bm, bn, bk, s, w, cg) <= 232448
