@@ -193,6 +193,20 @@ int ridge_gemm_host(const ridge_tile_config* cfg, const void* A, const void* B, 
                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                     int32_t panels, void* stream);
 
+/*
+ * ridge_gemm_launch that also stores every C tile into num_peers (<= 7) other
+ * M x N buffers with the same pitch ldc, typically copies of C in other GPUs'
+ * memory mapped into this process (ridge_ipc_open): the tile goes out once
+ * per destination from the same shared-memory staging, as part of the
+ * epilogue, so the copies overlap the math. Every destination must be
+ * 16-byte aligned with ldc a multiple of 8 (the TMA-store epilogue).
+ * No counterpart in the reference (single GPU); the building block of
+ * ridge_gemm_sharded_p2p.
+ */
+int ridge_gemm_launch_multi(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                            int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                            int64_t ldc, void* const* peer_c, int32_t num_peers, void* stream);
+
 /* Same, addressing the variant by its table index. */
 int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, int64_t M,
                               int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
@@ -412,6 +426,38 @@ int ridge_gemm_sharded(const ridge_tile_config* cfg, const void* A, const void* 
                        void* C_slab, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                        int32_t nranks, int32_t rank, int32_t gather_full_c, void* nccl_comm,
                        void* slabs, void* C_full, int64_t ldc_full, void* stream);
+
+/*
+ * The N-slab GEMM with the gather fused into the epilogue: rank `rank` of
+ * `nranks` (<= 8) computes its slab C[:, n0:n0+n_slab] and its epilogue stores
+ * every tile straight into all ranks' full M x N C buffers (c_full[r] for
+ * r = 0..nranks-1, this rank's own included, all with pitch ldc), over NVLink
+ * for the peers. c_full holds device pointers valid in this process (peers'
+ * from ridge_ipc_open). When nccl_comm is given, a one-element all-reduce on
+ * `stream` after the kernel makes the call a completion barrier: when it is
+ * done on this rank, every rank's tiles have landed in this rank's C. No
+ * counterpart in the reference; replaces ridge_gemm_sharded's NCCL
+ * all-gather + re-layout with copies that overlap the GEMM.
+ */
+int ridge_gemm_sharded_p2p(const ridge_tile_config* cfg, const void* A, const void* B_slab,
+                           int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                           int32_t nranks, int32_t rank, void* const* c_full, int64_t ldc,
+                           void* nccl_comm, void* stream);
+
+/*
+ * Device memory another process on this node can map (CUDA IPC), for the
+ * peer copies of C. ridge_device_alloc / ridge_device_free wrap cudaMalloc /
+ * cudaFree (an IPC handle names a whole allocation); ridge_ipc_export writes
+ * the handle (ridge_ipc_handle_bytes() bytes) of such an allocation;
+ * ridge_ipc_open maps another process's handle here (peer access enabled);
+ * ridge_ipc_close unmaps it.
+ */
+int64_t ridge_ipc_handle_bytes(void);
+int ridge_device_alloc(int64_t bytes, void** ptr);
+int ridge_device_free(void* ptr);
+int ridge_ipc_export(const void* base, void* handle);
+int ridge_ipc_open(const void* handle, void** ptr);
+int ridge_ipc_close(void* ptr);
 
 #ifdef __cplusplus
 }

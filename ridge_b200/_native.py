@@ -112,6 +112,17 @@ SIGNATURES = {
                                      _i64, _i64, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp,
                                      _i64, _vp]),
     "ridge_selftest_wait_timeout": (C.c_int, [_i64, C.POINTER(C.c_int32), C.POINTER(_i64)]),
+    "ridge_gemm_launch_multi": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
+                                          _i64, _i64, _i64, C.POINTER(_vp), C.c_int32, _vp]),
+    "ridge_gemm_sharded_p2p": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _i64, _i64, _i64, _i64,
+                                         _i64, C.c_int32, C.c_int32, C.POINTER(_vp), _i64, _vp,
+                                         _vp]),
+    "ridge_ipc_handle_bytes": (_i64, []),
+    "ridge_device_alloc": (C.c_int, [_i64, C.POINTER(_vp)]),
+    "ridge_device_free": (C.c_int, [_vp]),
+    "ridge_ipc_export": (C.c_int, [_vp, _vp]),
+    "ridge_ipc_open": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "ridge_ipc_close": (C.c_int, [_vp]),
     "ridge_gemm_host": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                   _i64, _i64, C.c_int32, _vp]),
     "ridge_gemm_launch_variant": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64,

@@ -427,7 +427,8 @@ int cached_workspace(int device, cudaStream_t stream, size_t bytes, void** out) 
 
 int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, void* C, int64_t M,
                   int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream_v,
-                  bool caller_ws, void* workspace, int64_t workspace_bytes) {
+                  bool caller_ws, void* workspace, int64_t workspace_bytes,
+                  void* const* peer_c = nullptr, int num_peers = 0) {
     int st = ridge_config_valid_for_shape(cfg, M, N, K, lda, ldb, ldc);
     if (st != RIDGE_OK) return st;
     if (M == 0 || N == 0) return RIDGE_OK;
@@ -438,8 +439,11 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
     DeviceState* dev = device_state(&st);
     if (!dev) return st;
+    if (num_peers < 0 || num_peers > kMaxPeers || (num_peers > 0 && !peer_c)) return RIDGE_EINVAL;
     if (K == 0) {
         cudaError_t e = cudaMemset2DAsync(C, size_t(ldc) * 2, 0, size_t(N) * 2, size_t(M), stream);
+        for (int d = 0; d < num_peers && e == cudaSuccess; ++d)
+            e = cudaMemset2DAsync(peer_c[d], size_t(ldc) * 2, 0, size_t(N) * 2, size_t(M), stream);
         return int(e);
     }
     LaunchPlan plan;
@@ -475,6 +479,16 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
         st = make_output_map(&tmap_c, C, M, N, ldc, e->epi_rows, e->epi_cols);
         if (st != RIDGE_OK) return st;
     }
+    // Peer copies of C take the same tile stores through their own maps, so
+    // they need the TMA-store epilogue (16-byte aligned, 16-byte pitch).
+    PeerMaps peers;
+    std::memset(&peers, 0, sizeof(peers));
+    if (num_peers > 0 && !tma_store) return RIDGE_EINVAL;
+    for (int d = 0; d < num_peers; ++d) {
+        if (!peer_c[d] || (reinterpret_cast<uintptr_t>(peer_c[d]) & 15)) return RIDGE_EINVAL;
+        st = make_output_map(&peers.map[d], peer_c[d], M, N, ldc, e->epi_rows, e->epi_cols);
+        if (st != RIDGE_OK) return st;
+    }
 
     GemmParams p;
     p.C = static_cast<__half*>(C);
@@ -486,14 +500,15 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     p.stages = cfg->stages;
     p.tma_store = tma_store ? 1 : 0;
     p.epi_stride = plan.epi_stride;
+    p.num_peers = num_peers;
     p.err = dev->err_word;
     p.dp_tiles = plan.dp_tiles;
     p.sk_tiles = plan.sk_tiles;
     p.sk_splits = plan.sk_splits;
     p.counters = static_cast<int*>(ws);
     p.workspace = ws ? reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes) : nullptr;
-    cudaError_t ce = e->launch(&tmap_a, &tmap_b, &tmap_c, &p, plan.grid_units * e->cta_group,
-                               plan.smem, stream);
+    cudaError_t ce = e->launch(&tmap_a, &tmap_b, &tmap_c, &peers, &p,
+                               plan.grid_units * e->cta_group, plan.smem, stream);
     return int(ce);
 }
 
@@ -590,6 +605,13 @@ int ridge_gemm_launch_ws(const ridge_tile_config* cfg, const void* A, const void
                          void* workspace, int64_t workspace_bytes, void* stream) {
     return launch_common(cfg, A, B, C, M, N, K, lda, ldb, ldc, stream, true, workspace,
                          workspace_bytes);
+}
+
+int ridge_gemm_launch_multi(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                            int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                            int64_t ldc, void* const* peer_c, int32_t num_peers, void* stream) {
+    return launch_common(cfg, A, B, C, M, N, K, lda, ldb, ldc, stream, false, nullptr, 0, peer_c,
+                         num_peers);
 }
 
 int ridge_gemm_launch(const ridge_tile_config* cfg, const void* A, const void* B, void* C,

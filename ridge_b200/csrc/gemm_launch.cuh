@@ -11,8 +11,9 @@ namespace ridge_b200 {
 
 template <int BM, int BN, int BK, int W, int CG>
 cudaError_t launch_gemm(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
-                        const CUtensorMap* tmap_c, const GemmParams* params, int grid_ctas,
-                        int smem_bytes, cudaStream_t stream) {
+                        const CUtensorMap* tmap_c, const PeerMaps* peers,
+                        const GemmParams* params, int grid_ctas, int smem_bytes,
+                        cudaStream_t stream) {
     using T = GemmTraits<BM, BN, BK, W, CG>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(grid_ctas), 1, 1);
@@ -29,7 +30,7 @@ cudaError_t launch_gemm(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
         cfg.numAttrs = 1;
     }
     return cudaLaunchKernelEx(&cfg, ridge_gemm_sm100<BM, BN, BK, W, CG>, *tmap_a, *tmap_b,
-                              *tmap_c, *params);
+                              *tmap_c, *peers, *params);
 }
 
 template <int BM, int BN, int BK, int W, int CG>

@@ -11,10 +11,12 @@
 namespace ridge_b200 {
 
 struct GemmParams;
+struct PeerMaps;
 
 using LaunchFn = cudaError_t (*)(const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
-                                 const CUtensorMap* tmap_c, const GemmParams* params,
-                                 int grid_ctas, int smem_bytes, cudaStream_t stream);
+                                 const CUtensorMap* tmap_c, const PeerMaps* peers,
+                                 const GemmParams* params, int grid_ctas, int smem_bytes,
+                                 cudaStream_t stream);
 
 struct KernelEntry {
     int BM, BN, BK, warps, cta_group;

@@ -112,6 +112,14 @@ struct GemmTraits {
     }
 };
 
+// Extra destinations of every C tile: the same tile coordinates stored through
+// each of these maps too (another GPU's copy of C, over NVLink). Used by the
+// fused N-slab GEMM + all-gather; empty for an ordinary launch.
+constexpr int kMaxPeers = 7;
+struct PeerMaps {
+    CUtensorMap map[kMaxPeers];
+};
+
 struct GemmParams {
     __half* C;
     int M, N, K;
@@ -120,6 +128,7 @@ struct GemmParams {
     int stages;
     int tma_store;  // 1: epilogue stores through the C tensor map; 0: direct st.global
     int epi_stride; // staging bytes per epilogue warp: 4096, or 8192 for two pair buffers
+    int num_peers;  // destinations in PeerMaps besides tmap_c (TMA-store epilogue only)
     int* err;
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
     // one per unit per round; the remaining sk_tiles tiles are each split into
@@ -193,7 +202,8 @@ template <int BM, int BN, int BK, int WARPS, int CG>
 __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     ridge_gemm_sm100(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b,
-                     const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmap_c,
+                     const __grid_constant__ PeerMaps peers, const GemmParams p) {
     using T = GemmTraits<BM, BN, BK, WARPS, CG>;
     extern __shared__ uint8_t smem_raw[];
 
@@ -236,6 +246,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         tma_prefetch_desc(&tmap_a);
         tma_prefetch_desc(&tmap_b);
         if (p.tma_store) tma_prefetch_desc(&tmap_c);
+        for (int d = 0; d < p.num_peers; ++d) tma_prefetch_desc(&peers.map[d]);
     }
     if (warp == 1) {
         tmem_alloc<CG>(smem_u32(tmem_slot), T::kTmemCols);
@@ -549,6 +560,9 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                     __syncwarp();
                     if (lane == buf) {
                         tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0);
+#pragma unroll 1
+                        for (int d = 0; d < p.num_peers; ++d)
+                            tma_store_2d(&peers.map[d], sbuf, col0, tile_row0 + warp_row0);
                         tma_store_commit();
                     }
                     buf ^= 1;
@@ -611,6 +625,9 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0_of(ci));
+#pragma unroll 1
+                    for (int d = 0; d < p.num_peers; ++d)
+                        tma_store_2d(&peers.map[d], sbuf, col0, tile_row0 + warp_row0_of(ci));
                     tma_store_commit();
                 }
                 ++pidx;

@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/ridge_b200.h"
@@ -66,15 +67,29 @@ __global__ void slabs_to_rowmajor_scalar(const uint16_t* __restrict__ slabs,
 // library does not link NCCL itself.
 using AllGatherFn = ncclResult_t (*)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
                                      cudaStream_t);
-AllGatherFn nccl_allgather() {
+using AllReduceFn = ncclResult_t (*)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                                     ncclComm_t, cudaStream_t);
+void* nccl_symbol(const char* name) {
     static std::once_flag once;
-    static AllGatherFn fn = nullptr;
+    static void* lib = nullptr;
     std::call_once(once, [] {
-        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
-        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-        if (h) fn = reinterpret_cast<AllGatherFn>(dlsym(h, "ncclAllGather"));
+        lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     });
-    return fn;
+    return lib ? dlsym(lib, name) : nullptr;
+}
+AllGatherFn nccl_allgather() { return reinterpret_cast<AllGatherFn>(nccl_symbol("ncclAllGather")); }
+AllReduceFn nccl_allreduce() { return reinterpret_cast<AllReduceFn>(nccl_symbol("ncclAllReduce")); }
+
+// One int per device for the completion barrier's all-reduce.
+int* barrier_word() {
+    static std::mutex mu;
+    static int* words[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!words[dev] && cudaMalloc(&words[dev], sizeof(int)) != cudaSuccess) words[dev] = nullptr;
+    return words[dev];
 }
 
 }  // namespace
@@ -147,5 +162,65 @@ int ridge_gemm_sharded(const ridge_tile_config* cfg, const void* A, const void* 
         return RIDGE_ECOMM;
     return ridge_slabs_to_rowmajor(slabs, C_full, M, N, nranks, per, ldc_full, stream);
 }
+
+int ridge_gemm_sharded_p2p(const ridge_tile_config* cfg, const void* A, const void* B_slab,
+                           int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                           int32_t nranks, int32_t rank, void* const* c_full, int64_t ldc,
+                           void* nccl_comm, void* stream) {
+    constexpr int64_t kAlign = 256;
+    if (!cfg || !c_full || M < 0 || N < 0 || K < 0 || nranks < 1 || nranks > 8 || ldc < N)
+        return RIDGE_EINVAL;
+    int64_t n0 = 0, ns = 0;
+    int st = ridge_slab_bounds(N, nranks, rank, kAlign, &n0, &ns);
+    if (st != RIDGE_OK) return st;
+    if (M > 0 && ns > 0) {
+        // this rank's slab of every rank's C: the same tile coordinates,
+        // offset by n0 columns in each buffer
+        void* peers[8];
+        int np = 0;
+        for (int r = 0; r < nranks; ++r) {
+            if (!c_full[r]) return RIDGE_EINVAL;
+            if (r != rank) peers[np++] = static_cast<__half*>(c_full[r]) + n0;
+        }
+        st = ridge_gemm_launch_multi(cfg, A, B_slab, static_cast<__half*>(c_full[rank]) + n0, M,
+                                     ns, K, lda, ldb, ldc, peers, np, stream);
+        if (st != RIDGE_OK) return st;
+    }
+    if (!nccl_comm || nranks == 1) return RIDGE_OK;
+    AllReduceFn ar = nccl_allreduce();
+    int* word = barrier_word();
+    if (!ar || !word) return RIDGE_ECOMM;
+    if (ar(word, word, 1, ncclInt32, ncclSum, static_cast<ncclComm_t>(nccl_comm),
+           static_cast<cudaStream_t>(stream)) != ncclSuccess)
+        return RIDGE_ECOMM;
+    return RIDGE_OK;
+}
+
+int64_t ridge_ipc_handle_bytes(void) { return int64_t(sizeof(cudaIpcMemHandle_t)); }
+
+int ridge_device_alloc(int64_t bytes, void** ptr) {
+    if (bytes <= 0 || !ptr) return RIDGE_EINVAL;
+    return int(cudaMalloc(ptr, size_t(bytes)));
+}
+
+int ridge_device_free(void* ptr) { return int(cudaFree(ptr)); }
+
+int ridge_ipc_export(const void* base, void* handle) {
+    if (!base || !handle) return RIDGE_EINVAL;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(base));
+    if (e != cudaSuccess) return int(e);
+    std::memcpy(handle, &h, sizeof(h));
+    return RIDGE_OK;
+}
+
+int ridge_ipc_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return RIDGE_EINVAL;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return int(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int ridge_ipc_close(void* ptr) { return int(cudaIpcCloseMemHandle(ptr)); }
 
 }  // extern "C"

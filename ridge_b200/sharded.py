@@ -114,6 +114,84 @@ def sharded_gemm(a, b, config: TileConfig, gather: bool = False, group=None, ran
     return c_slab[:, :ns], full
 
 
+class PeerC:
+    """Every rank's full M x N C, mapped into every rank's process: allocated
+    here with ridge_device_alloc (CUDA IPC needs a whole allocation),
+    handles exchanged over the process group, peers' buffers opened with
+    ridge_ipc_open. `ptrs` is the device-pointer array ridge_gemm_sharded_p2p
+    takes; `local` is this rank's C as a torch tensor (no copy)."""
+
+    def __init__(self, M: int, N: int, group=None):
+        import torch
+        import torch.distributed as dist
+        self.M, self.N = M, N
+        self.ldc = max(8, (N + 7) // 8 * 8)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        base = C.c_void_p()
+        check(lib.ridge_device_alloc(M * self.ldc * 2, C.byref(base)), "ridge_device_alloc")
+        self._base = base.value
+        nb = lib.ridge_ipc_handle_bytes()
+        h = (C.c_char * nb)()
+        check(lib.ridge_ipc_export(self._base, h), "ridge_ipc_export")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        self._opened = []
+        ptrs = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._base)
+                continue
+            p = C.c_void_p()
+            check(lib.ridge_ipc_open(C.create_string_buffer(hb, nb), C.byref(p)),
+                  "ridge_ipc_open rank %d" % r)
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.ptrs = (C.c_void_p * self.world)(*ptrs)
+        buf = self
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (M, N), "strides": (self.ldc * 2, 2),
+                                        "typestr": "<f2", "data": (buf._base, False),
+                                        "version": 3}
+        self.local = torch.as_tensor(_View(), device=torch.device("cuda",
+                                                                  torch.cuda.current_device()))
+
+    def close(self, group=None):
+        """Collective: unmap the peers' buffers, wait until every rank has
+        unmapped this rank's, then free it."""
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        for p in self._opened:
+            lib.ridge_ipc_close(p)
+        self._opened = []
+        dist.barrier(group=group)
+        if self._base:
+            lib.ridge_device_free(self._base)
+            self._base = None
+
+
+def sharded_gemm_p2p(a, b_slab, config: TileConfig, peer_c: PeerC, group=None, barrier=True,
+                     stream=None):
+    """This rank's slab GEMM with the gather fused into its epilogue: every
+    tile lands in every rank's C (peer_c) directly. With barrier=True the call
+    ends with a one-element all-reduce on `stream`, after which this rank's C
+    holds every rank's slab."""
+    M, K = a.shape
+    N = peer_c.N
+    cc = config.to_c()
+    comm = nccl_comm_ptr(group) if barrier and peer_c.world > 1 else None
+    ns = b_slab.shape[0]
+    st = lib.ridge_gemm_sharded_p2p(C.byref(cc), a.data_ptr(),
+                                    b_slab.data_ptr() if ns else a.data_ptr(), M, N, K,
+                                    max(a.stride(0), 1), max(b_slab.stride(0), 1) if ns else K,
+                                    peer_c.world, peer_c.rank, peer_c.ptrs, peer_c.ldc, comm,
+                                    _stream_handle(stream))
+    check(st, "ridge_gemm_sharded_p2p %dx%dx%d rank %d/%d" % (M, N, K, peer_c.rank, peer_c.world))
+    return peer_c.local
+
+
 def main(argv=None):
     """Whole-node TFLOP/s of an N-slab GEMM: device time of `steps` slab GEMMs
     per rank (CUDA events), max over ranks; optionally the gather separately."""
@@ -128,6 +206,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--gather", action="store_true")
+    ap.add_argument("--fused", action="store_true",
+                    help="also time the GEMM with the gather fused into its epilogue (P2P)")
     ap.add_argument("--timeout", type=float, default=120.0,
                     help="seconds before a stuck collective is aborted")
     a = ap.parse_args(argv)
@@ -190,12 +270,35 @@ def main(argv=None):
         dist.all_reduce(g, op=dist.ReduceOp.MAX)
         step_ms = float(g.item())
         gather_ms = step_ms - float(t.item())
+    fused_ms = None
+    if a.fused and world > 1:
+        pc = PeerC(M, N)
+        Bv = B  # this rank's slab rows
+
+        def fstep():
+            sharded_gemm_p2p(A, Bv, cfg, pc)
+
+        for _ in range(2):
+            fstep()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record()
+        for _ in range(a.steps):
+            fstep()
+        e1.record()
+        torch.cuda.synchronize()
+        g = torch.tensor([e0.elapsed_time(e1) / a.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(g, op=dist.ReduceOp.MAX)
+        fused_ms = float(g.item())
+        pc.close()
     if rank == 0:
         tflops = 2.0 * M * N * K / (float(t.item()) * 1e-3) / 1e12
         print(json.dumps({"workload": "%dx%dx%d N-slab over %d GPU(s)" % (M, N, K, world),
                           "config": cfg.tag(), "ms_per_gemm_max_over_ranks": float(t.item()),
                           "tflops_whole_node": tflops, "ms_gemm_plus_gather": step_ms,
-                          "gather_ms": gather_ms}))
+                          "gather_ms": gather_ms, "ms_gemm_fused_gather": fused_ms,
+                          "tflops_fused_with_gather": (2.0 * M * N * K / (fused_ms * 1e-3) / 1e12
+                                                       if fused_ms else None)}))
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -59,3 +59,55 @@ def test_two_rank_sharded_gemm_gathers_the_whole_c():
         p.join(timeout=300)
     results = dict(q.get(timeout=5) for _ in procs)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def _worker_p2p(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import ridge_b200 as rb
+    from ridge_b200.sharded import PeerC, sharded_gemm, sharded_gemm_p2p, slab_bounds
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    try:
+        for cfg in (rb.TileConfig(128, 256, 64, 4, 4, 8), rb.TileConfig(256, 256, 64, 5, 4, 8, 2)):
+            for (M, N, K) in SHAPES + [(1000, 1536, 512)]:
+                a, b = rb.synthetic_inputs(M, N, K, device=dev)
+                n0, ns = slab_bounds(N, world, rank)
+                pc = PeerC(M, N)
+                pc.local.fill_(float("nan"))
+                torch.cuda.synchronize()
+                dist.barrier()
+                full = sharded_gemm_p2p(a, b[n0:n0 + ns], cfg, pc)
+                _, ref = sharded_gemm(a, b, cfg, gather=True)   # NCCL all-gather path
+                torch.cuda.synchronize()
+                assert rb.device_error() == 0
+                assert torch.equal(full, ref), (rank, cfg.tag(), M, N, K)
+                pc.close()
+        q.put((rank, "ok"))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_fused_p2p_gather_matches_the_nccl_gather():
+    """ridge_gemm_sharded_p2p: every rank's epilogue writes its tiles into both
+    ranks' C over NVLink; after the completion barrier each rank's C equals the
+    NCCL all-gather result bit for bit (same slab GEMMs)."""
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_p2p, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    results = dict(q.get(timeout=5) for _ in procs)
+    assert results == {0: "ok", 1: "ok"}, results
