@@ -596,10 +596,13 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             auto store_pair = [&](int ci, const uint32_t (&pa)[16], const uint32_t (&pb)[16]) {
                 const int j = group * kPerHalf + ci % kPerHalf;
                 const int col0 = tn * BN + j * 32;
-                // one buffer: the previous pair's store (issued by lane 0) has
-                // read it; two: the store before that one has read this one
+                // Destination d (0: this C, d > 0: peer d - 1) is stored by lane
+                // d, so the copies to other GPUs leave in parallel. One buffer:
+                // the previous pair's stores have read it; two: the stores
+                // before those have read this one (each issuing lane waits on
+                // its own stores).
                 const uint32_t sbuf = stage_buf0 + (two_pair_bufs ? (pidx & 1u) * 4096u : 0u);
-                if (lane == 0) {
+                if (lane <= p.num_peers) {
                     if (two_pair_bufs)
                         tma_store_wait_read<1>();
                     else
@@ -623,11 +626,10 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0_of(ci));
-#pragma unroll 1
-                    for (int d = 0; d < p.num_peers; ++d)
-                        tma_store_2d(&peers.map[d], sbuf, col0, tile_row0 + warp_row0_of(ci));
+                if (lane <= p.num_peers) {
+                    tma_store_2d(lane == 0 ? static_cast<const void*>(&tmap_c)
+                                           : static_cast<const void*>(&peers.map[lane - 1]),
+                                 sbuf, col0, tile_row0 + warp_row0_of(ci));
                     tma_store_commit();
                 }
                 ++pidx;
@@ -697,7 +699,8 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 acc_phase ^= 1u;
             }
         }
-        if (p.tma_store && lane < 2) tma_store_wait_all<0>();  // lanes 0 and 1 issue stores
+        // lanes 0 and 1 issue chunk stores, lanes 0..num_peers pair stores
+        if (p.tma_store && (lane < 2 || lane <= p.num_peers)) tma_store_wait_all<0>();
     }
 
     tc_fence_before();
