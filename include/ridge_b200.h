@@ -131,7 +131,10 @@ int ridge_gemm_workspace_size(const ridge_tile_config* cfg, int64_t M, int64_t N
  * ridge_gemm_workspace_size bytes (256-byte aligned). Its first 64 KB are the
  * split-K counter area, which must be zero before the first launch (e.g.
  * cudaMemset once); every launch leaves it zero again, so one workspace can
- * serve any sequence of configs and shapes. Launches that share one workspace must be ordered (one stream).
+ * serve any sequence of configs and shapes. Launches that share one workspace
+ * must be ordered (one stream); launches with separate workspaces may overlap
+ * freely (a split tile is reduced by whichever split arrives last, and no
+ * CTA waits on another).
  * ridge_gemm_launch itself keeps such a workspace per device and stream.
  */
 int ridge_gemm_launch_ws(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
@@ -168,6 +171,17 @@ int ridge_gemm_launch_noalloc(const ridge_tile_config* cfg, const void* A, const
  * Synchronises the device. RIDGE_EDEVICE if the wait did not give up.
  */
 int ridge_selftest_wait_timeout(int64_t limit_ns, int32_t* code, int64_t* waited_ns);
+
+/*
+ * Self-test of the recovery path (no counterpart in the reference): leaves the
+ * current device in the state a GEMM that gave up mid-launch can leave behind
+ * -- every byte of the split-K counter areas the library owns (its cached
+ * workspaces and the no-allocation scratch, where set up) set to `byte`
+ * (1..255) and the device error word set to code 7 -- without running a
+ * kernel. ridge_device_error(1, ...) must then restore a state in which split
+ * launches are correct again. Synchronises the device.
+ */
+int ridge_selftest_stale_counters(int32_t byte);
 
 /* Size in bytes of ridge_gemm_launch_noalloc's fixed per-device scratch. No counterpart in
  * the reference. */
@@ -215,6 +229,10 @@ int ridge_gemm_launch_variant(int index, const void* A, const void* B, void* C, 
 /*
  * Reads (and, when clear != 0, resets) the device-side error word of the
  * current device after synchronising it. *code = 0 when no kernel timed out.
+ * Clearing a non-zero word also zeroes the split-K counter areas of every
+ * workspace the library owns on the device (the cached ones and the
+ * no-allocation scratch), which a kernel that gave up may have left non-zero;
+ * caller-owned workspaces (ridge_gemm_launch_ws) are the caller's to re-zero.
  * Returns RIDGE_OK, or a CUDA error from the synchronisation.
  */
 int ridge_device_error(int clear, int32_t* code);
@@ -433,9 +451,15 @@ int ridge_gemm_sharded(const ridge_tile_config* cfg, const void* A, const void* 
  * every tile straight into all ranks' full M x N C buffers (c_full[r] for
  * r = 0..nranks-1, this rank's own included, all with pitch ldc), over NVLink
  * for the peers. c_full holds device pointers valid in this process (peers'
- * from ridge_ipc_open). When nccl_comm is given, a one-element all-reduce on
- * `stream` after the kernel makes the call a completion barrier: when it is
- * done on this rank, every rank's tiles have landed in this rank's C. No
+ * from ridge_ipc_open). When nccl_comm is given, the call is fenced on both
+ * sides by a one-element all-reduce on `stream`: the one before the kernel is
+ * an entry barrier (no rank starts writing into the others' C until every
+ * rank has reached this call in its stream order, so work a rank enqueued on
+ * `stream` before the call -- reading its previous C, say -- is finished
+ * first), the one after it a completion barrier (when it is done on this
+ * rank, every rank's tiles have landed in this rank's C). A rank that reads
+ * its C on another stream or on the host must finish doing so before it makes
+ * the next call. Without nccl_comm the caller provides both fences. No
  * counterpart in the reference; replaces ridge_gemm_sharded's NCCL
  * all-gather + re-layout with copies that overlap the GEMM.
  */

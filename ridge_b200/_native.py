@@ -112,6 +112,7 @@ SIGNATURES = {
                                      _i64, _i64, C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp,
                                      _i64, _vp]),
     "ridge_selftest_wait_timeout": (C.c_int, [_i64, C.POINTER(C.c_int32), C.POINTER(_i64)]),
+    "ridge_selftest_stale_counters": (C.c_int, [C.c_int32]),
     "ridge_gemm_launch_multi": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
                                           _i64, _i64, _i64, C.POINTER(_vp), C.c_int32, _vp]),
     "ridge_gemm_sharded_p2p": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _i64, _i64, _i64, _i64,

@@ -25,6 +25,8 @@
 
 namespace ridge_b200 {
 
+int noalloc_fill_counters(int byte);  // gemm_noalloc.cu
+
 // Per-device error word written by kernels whose bounded waits expire.
 __device__ int g_ridge_device_err = 0;
 
@@ -207,8 +209,8 @@ int smem_for(const KernelEntry& e, int stages) { return e.fixed_smem + stages * 
 // Dynamic shared memory a launch requests. When shared memory alone would let
 // more CTAs share an SM than Tensor Memory can hold, the request is padded so
 // the hardware never co-schedules a CTA whose tcgen05.alloc would have to
-// wait for another CTA to exit: split-K owners wait on other CTAs' partials,
-// so every CTA of the grid must be able to run at once.
+// wait for another CTA to exit: such a CTA would only idle on its SM, and the
+// grid is sized to the CTAs that can run at once.
 int launch_smem(const KernelEntry& e, int stages) {
     int smem = e.fixed_smem + stages * e.stage_bytes;
     const int by_tmem = kTmemColsPerSm / e.tmem_cols;
@@ -377,7 +379,8 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     plan->grid_units = int(std::max<int64_t>(std::min(tiles, units), rem * s));
     // Workspace: [counters: kCounterBytes][FP32 partial tiles]. The counter
     // area sits at a fixed offset so that every config sharing a workspace
-    // finds it zeroed (owners reset their counters; partials never overlap it).
+    // finds it zeroed (the last arrival resets each counter; partials never
+    // overlap it).
     if (rem * e->cta_group * e->warps * 4 > kCounterBytes) {
         plan->dp_tiles = int(tiles);
         plan->sk_tiles = 0;
@@ -386,7 +389,7 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
         return RIDGE_OK;
     }
     const size_t tile_floats = size_t(e->partial_floats);
-    plan->ws_partials = size_t(rem) * (s - 1) * e->cta_group * tile_floats * 4;
+    plan->ws_partials = size_t(rem) * s * e->cta_group * tile_floats * 4;  // one slot per split
     plan->ws_bytes = kCounterBytes + plan->ws_partials;
     return RIDGE_OK;
 }
@@ -510,6 +513,24 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     cudaError_t ce = e->launch(&tmap_a, &tmap_b, &tmap_c, &peers, &p,
                                plan.grid_units * e->cta_group, plan.smem, stream);
     return int(ce);
+}
+
+// Sets every byte of the split-K counter areas this library owns on the current
+// device (cached workspaces, the no-allocation scratch) to `byte`.
+int fill_library_counters(int byte) {
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return int(e);
+    {
+        WorkspaceCache& c = g_ws[device];
+        std::lock_guard<std::mutex> lock(c.mu);
+        for (auto& kv : c.by_stream) {
+            if (!kv.second.first) continue;
+            e = cudaMemset(kv.second.first, byte, size_t(kCounterBytes));
+            if (e != cudaSuccess) return int(e);
+        }
+    }
+    return noalloc_fill_counters(byte);
 }
 
 }  // namespace
@@ -669,15 +690,24 @@ int ridge_device_error(int clear, int32_t* code) {
     if (clear && v != 0) {
         e = cudaMemset(dev->err_word, 0, sizeof(int));
         if (e != cudaSuccess) return int(e);
-        // A kernel that gave up may have left split-K counters non-zero.
-        int device = 0;
-        cudaGetDevice(&device);
-        WorkspaceCache& c = g_ws[device];
-        std::lock_guard<std::mutex> lock(c.mu);
-        for (auto& kv : c.by_stream)
-            if (kv.second.first) cudaMemset(kv.second.first, 0, size_t(kCounterBytes));
+        // A kernel that gave up may have left split-K counters non-zero: in
+        // the library's cached workspaces and in the no-allocation scratch.
+        if ((st = fill_library_counters(0)) != RIDGE_OK) return st;
     }
     return RIDGE_OK;
+}
+
+int ridge_selftest_stale_counters(int32_t byte) {
+    if (byte < 1 || byte > 255) return RIDGE_EINVAL;
+    int st = RIDGE_OK;
+    DeviceState* dev = device_state(&st);
+    if (!dev) return st;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return int(e);
+    if ((st = fill_library_counters(byte)) != RIDGE_OK) return st;
+    const int code = kErrSelfTestStale;
+    e = cudaMemcpy(dev->err_word, &code, sizeof(int), cudaMemcpyHostToDevice);
+    return int(e);
 }
 
 }  // extern "C"

@@ -61,6 +61,23 @@ int scratch_for_current_device(void** out) {
 
 }  // namespace
 
+namespace ridge_b200 {
+
+// Sets every byte of the scratch's split-K counter area on the current device
+// to `byte`, if that device's scratch was set up. ridge_device_error(clear)
+// calls it with 0 after a kernel gave up mid-launch (its counters may be left
+// non-zero, and the next split launch would then never find its last
+// arrival); the self-test plants non-zero counters with it.
+int noalloc_fill_counters(int byte) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return int(e);
+    if (dev < 0 || dev >= kMaxDevices || !g_slot[dev].ptr) return RIDGE_OK;
+    return int(cudaMemset(g_slot[dev].ptr, byte, size_t(kCounterAreaBytes)));
+}
+
+}  // namespace ridge_b200
+
 extern "C" {
 
 int64_t ridge_gemm_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }

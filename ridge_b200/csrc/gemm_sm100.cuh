@@ -133,10 +133,11 @@ struct GemmParams {
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
     // one per unit per round; the remaining sk_tiles tiles are each split into
     // sk_splits contiguous K ranges, one range per unit, in a single last
-    // round. Split 0 of a tile owns it: it adds the FP32 partials the other
-    // splits leave in `workspace` and stores C. counters[(sk * CG + rank) *
-    // warps + warp] counts partial chunks published for one owner warp; the
-    // owner resets it to 0 after consuming, so it starts at 0 every launch.
+    // round. Every split publishes its FP32 partial into its own slot of
+    // `workspace` and then takes a ticket from counters[(sk * CG + rank) *
+    // warps + warp]; the warp holding the last ticket adds all slots in split
+    // order and stores C, then resets the counter to 0, so it starts at 0
+    // every launch. No split ever waits for another.
     int dp_tiles;
     int sk_tiles;
     int sk_splits;
@@ -170,12 +171,6 @@ __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_
         return true;
     }
     return false;
-}
-
-__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-    return v;
 }
 
 // Grouped-M tile order, the same mapping as the reference launch order
@@ -436,31 +431,17 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            // Split-K bookkeeping for this item: where this CTA's FP32 partial
-            // tiles live, and (owner) the counter its partial chunks bump.
+            // Split-K bookkeeping for this item: where the tile's FP32 partial
+            // slots live (one per split, in split order) and the counter that
+            // tickets this warp's arrivals.
             constexpr long long kTileFloats = T::kPartialFloats;
             float* ws_tile = nullptr;
             int* counter = nullptr;
             if (w.split >= 0) {
                 counter = p.counters + (w.sk * CG + int(rank)) * WARPS + epi;
-                const long long slot0 = (long long)w.sk * (p.sk_splits - 1);
+                const long long slot0 = (long long)w.sk * p.sk_splits;
                 ws_tile = p.workspace + (slot0 * CG + rank) * kTileFloats;
             }
-            if (w.split == 0 && lane == 0) {
-                // Owner: wait until every other split published this warp's chunks.
-                const int want = p.sk_splits - 1;
-                if (ld_acquire_gpu(counter) < want) {
-                    const uint64_t t0 = global_timer_ns();
-                    while (ld_acquire_gpu(counter) < want) {
-                        if (global_timer_ns() - t0 > RIDGE_WAIT_LIMIT_NS) {
-                            *abort_flag = 1;
-                            atomicCAS(p.err, 0, int(kErrTimeoutSplitK));
-                            break;
-                        }
-                    }
-                }
-            }
-            __syncwarp();
             // This warp's chunks of the tile are drained kLd at a time:
             // both TMEM loads are issued before one wait (tcgen05.wait::ld
             // waits for all of a thread's loads), and the next group's loads
@@ -483,7 +464,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             // Split-K partial chunks use a lane-contiguous layout: float4 v of
             // lane L of chunk c sits at ((c * 8 + v) * 32 + L), so every
             // warp-wide store or load covers 512 contiguous bytes. Producer
-            // and owner map warps to chunks identically.
+            // and folding warps map warps to chunks identically.
             auto ws_offset = [&](int ci) {
                 const int h = ci / kPerHalf, j = group * kPerHalf + ci % kPerHalf;
                 const long long chunk_id = (long long)(h * kChunks + j) * 4 + quad;
@@ -499,10 +480,10 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 return (long long)tile_row0 + warp_row0_of(ci) < p.M;
             };
             auto publish = [&](int ci, const uint32_t (&r)[32]) {
-                // Non-owner split: publish the FP32 partial chunk.
+                // Publish this split's FP32 partial chunk into its slot.
                 if (!warp_live_of(ci)) return;
                 float4* dst = reinterpret_cast<float4*>(
-                    ws_tile + (long long)(w.split - 1) * CG * kTileFloats + ws_offset(ci));
+                    ws_tile + (long long)w.split * CG * kTileFloats + ws_offset(ci));
 #pragma unroll
                 for (int v = 0; v < 8; ++v)
                     __stcg(dst + v * 32, make_float4(__uint_as_float(r[4 * v]),
@@ -510,27 +491,44 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                                                      __uint_as_float(r[4 * v + 2]),
                                                      __uint_as_float(r[4 * v + 3])));
             };
-            auto fold_and_pack = [&](int ci, uint32_t (&r)[32], uint32_t (&packed)[16]) {
-                if (w.split == 0 && warp_live_of(ci)) {
-                    // Owner: add the other splits' partials, in split order.
-                    for (int sp = 1; sp < p.sk_splits; ++sp) {
+            auto pack = [&](const uint32_t (&r)[32], uint32_t (&packed)[16]) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+            };
+            // Last arrival of a split tile: the sum of every split's partial,
+            // added in split order (the same order whichever split arrives last,
+            // so the result is deterministic), packed to FP16.
+            auto fold_ws = [&](int ci, uint32_t (&packed)[16]) {
+                float4 acc[8];
+#pragma unroll
+                for (int v = 0; v < 8; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (warp_live_of(ci)) {
+                    for (int sp = 0; sp < p.sk_splits; ++sp) {
                         const float4* src = reinterpret_cast<const float4*>(
-                            ws_tile + (long long)(sp - 1) * CG * kTileFloats + ws_offset(ci));
+                            ws_tile + (long long)sp * CG * kTileFloats + ws_offset(ci));
                         float4 q[8];
 #pragma unroll
                         for (int v = 0; v < 8; ++v) q[v] = __ldcg(src + v * 32);
+                        if (sp == 0) {
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) {
-                            r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q[v].x);
-                            r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q[v].y);
-                            r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q[v].z);
-                            r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q[v].w);
+                            for (int v = 0; v < 8; ++v) acc[v] = q[v];
+                        } else {
+#pragma unroll
+                            for (int v = 0; v < 8; ++v) {
+                                acc[v].x += q[v].x;
+                                acc[v].y += q[v].y;
+                                acc[v].z += q[v].z;
+                                acc[v].w += q[v].w;
+                            }
                         }
                     }
                 }
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                for (int v = 0; v < 8; ++v) {
+                    packed[2 * v] = pack_half2(acc[v].x, acc[v].y);
+                    packed[2 * v + 1] = pack_half2(acc[v].z, acc[v].w);
+                }
             };
             auto store_chunk = [&](int ci, const uint32_t (&packed)[16]) {
                 const int j = group * kPerHalf + ci % kPerHalf;
@@ -643,28 +641,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 tmem_wait_ld(ra);
                 if constexpr (kLd == 2) tmem_wait_ld(rb);
             };
-            load_group(0);
-            wait_group();
-#pragma unroll 1
-            for (int ci = 0; ci < kPerWarp; ci += kLd) {
-                const bool more = ci + kLd < kPerWarp;
-                if (w.split > 0) {
-                    publish(ci, ra);
-                    if constexpr (kLd == 2) publish(ci + 1, rb);
-                    if (more) {
-                        __syncwarp();
-                        load_group(ci + kLd);
-                        wait_group();
-                    }
-                    continue;  // warp-uniform: w.split is the same on every lane
-                }
-                uint32_t pa[16], pb[16];
-                fold_and_pack(ci, ra, pa);
-                if constexpr (kLd == 2) fold_and_pack(ci + 1, rb, pb);
-                if (more) {
-                    __syncwarp();
-                    load_group(ci + kLd);  // lands while this group is stored
-                }
+            auto store_group = [&](int ci, const uint32_t (&pa)[16], const uint32_t (&pb)[16]) {
                 if constexpr (kLd == 2) {
                     if (p.tma_store) {
                         store_pair(ci, pa, pb);
@@ -675,24 +652,67 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 } else {
                     store_chunk(ci, pa);
                 }
-                if (more) wait_group();
-            }
-            if (w.split > 0) {
-                // Make this warp's partial chunks visible, then count them.
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) atomicAdd(counter, 1);
-            } else if (w.split == 0 && lane == 0) {
-                *counter = 0;  // consumed: ready for the next launch
-            }
+            };
             // Every TMEM read of this accumulator is done: hand it back.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if constexpr (CG == 1)
-                    mbar_arrive(tempty_bar(acc));
-                else
-                    mbar_arrive_cluster(tempty0 + 8u * acc);
+            auto release_acc = [&]() {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (CG == 1)
+                        mbar_arrive(tempty_bar(acc));
+                    else
+                        mbar_arrive_cluster(tempty0 + 8u * acc);
+                }
+            };
+            load_group(0);
+            wait_group();
+            if (w.split >= 0) {
+                // Split-K item (warp-uniform branch). Publish this split's
+                // partial, then take a ticket; the split whose ticket comes
+                // last folds every slot and stores C. Nobody waits on another
+                // CTA, so split ranges need not be resident at the same time.
+#pragma unroll 1
+                for (int ci = 0; ci < kPerWarp; ci += kLd) {
+                    publish(ci, ra);
+                    if constexpr (kLd == 2) publish(ci + 1, rb);
+                    if (ci + kLd < kPerWarp) {
+                        __syncwarp();
+                        load_group(ci + kLd);
+                        wait_group();
+                    }
+                }
+                release_acc();
+                __threadfence();  // this warp's partial is visible before its ticket
+                __syncwarp();
+                int ticket = 0;
+                if (lane == 0) ticket = atomicAdd(counter, 1);
+                ticket = __shfl_sync(0xffffffffu, ticket, 0);
+                if (ticket == p.sk_splits - 1) {
+                    __threadfence();  // the other splits' partials, published before their tickets
+#pragma unroll 1
+                    for (int ci = 0; ci < kPerWarp; ci += kLd) {
+                        uint32_t pa[16], pb[16];
+                        fold_ws(ci, pa);
+                        if constexpr (kLd == 2) fold_ws(ci + 1, pb);
+                        store_group(ci, pa, pb);
+                    }
+                    if (lane == 0) *counter = 0;  // every split arrived: ready for the next launch
+                }
+            } else {
+#pragma unroll 1
+                for (int ci = 0; ci < kPerWarp; ci += kLd) {
+                    const bool more = ci + kLd < kPerWarp;
+                    uint32_t pa[16], pb[16];
+                    pack(ra, pa);
+                    if constexpr (kLd == 2) pack(rb, pb);
+                    if (more) {
+                        __syncwarp();
+                        load_group(ci + kLd);  // lands while this group is stored
+                    }
+                    store_group(ci, pa, pb);
+                    if (more) wait_group();
+                }
+                release_acc();
             }
             if (++acc == T::kAccBufs) {
                 acc = 0;

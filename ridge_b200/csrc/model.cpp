@@ -245,13 +245,12 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     double t_unit = dp_per_unit * tile_period(t_main_whole);
     double t_sk = 0.0;
     if (splits >= 2) {
-        // One K range of 1/splits, then the owner folds in splits - 1 FP32
-        // partial tiles (read at the fill rate) before its epilogue.
+        // One K range of 1/splits; every split writes its FP32 partial
+        // (twice the bytes of an FP16 tile, at the drain rate), and the last
+        // to arrive reads all `splits` partials back before its epilogue.
         const double partial_bytes = double(g.rows_per_cta) * t.BN * 4.0;
-        // The owner cannot reduce before the other splits have written their
-        // FP32 partials (twice the bytes of an FP16 tile, at the drain rate).
         t_sk = std::ceil(kb / double(splits)) * t_period + partial_bytes / epi_bpc +
-               double(splits - 1) * partial_bytes / (2.0 * epi_bpc) + t_epi;
+               double(splits) * partial_bytes / (2.0 * epi_bpc) + t_epi;
         t_unit += t_sk;
     } else if (info.acc_buffers >= 2 && dp_per_unit > 0) {
         t_unit += std::min(t_main_whole, t_epi);  // the last tile's epilogue drains alone
@@ -263,7 +262,7 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     // ---- HBM: operand reads (grouped-M walk, L2 reuse), C writes, split-K partials
     const double c_write = double(M) * N * 2.0;
     const double partial_traffic =
-        splits >= 2 ? 2.0 * double(rem) * (splits - 1) * g.cg * double(g.rows_per_cta) * t.BN * 4.0
+        splits >= 2 ? 2.0 * double(rem) * splits * g.cg * double(g.rows_per_cta) * t.BN * 4.0
                     : 0.0;
     const double hbm_sec = a_b_reads / hw->hbm_bytes_per_sec + c_write / hw->c_write_bytes_per_sec +
                            partial_traffic / hw->c_write_bytes_per_sec + hw->launch_overhead_sec;

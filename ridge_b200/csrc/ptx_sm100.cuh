@@ -22,8 +22,9 @@ enum DeviceErr : int {
     kErrTimeoutMma = 2,        // MMA issuer waited too long for a full stage / free accumulator
     kErrTimeoutEpilogue = 3,   // epilogue waited too long for a finished accumulator
     kErrTimeoutDrain = 4,      // abort path: in-flight copies did not land in time
-    kErrTimeoutSplitK = 5,     // split-K owner waited too long for another split's partial
+    kErrTimeoutSplitK = 5,     // unused since split-K tiles fold on last arrival (kept: code values are stable)
     kErrSelfTest = 6,          // ridge_selftest_wait_timeout: the wait expired as intended
+    kErrSelfTestStale = 7,     // ridge_selftest_stale_counters: planted stale split-K counters
 };
 
 // Wall-clock budget for any single mbarrier wait, in nanoseconds. A healthy

@@ -173,6 +173,20 @@ int ridge_gemm_sharded_p2p(const ridge_tile_config* cfg, const void* A, const vo
     int64_t n0 = 0, ns = 0;
     int st = ridge_slab_bounds(N, nranks, rank, kAlign, &n0, &ns);
     if (st != RIDGE_OK) return st;
+    const bool fenced = nccl_comm && nranks > 1;
+    AllReduceFn ar = nullptr;
+    int* word = nullptr;
+    if (fenced) {
+        // Entry barrier: this rank's tiles go into every peer's C, so no rank
+        // may start before all ranks are done with what their streams held
+        // before this call (reading the previous result, typically).
+        ar = nccl_allreduce();
+        word = barrier_word();
+        if (!ar || !word) return RIDGE_ECOMM;
+        if (ar(word, word, 1, ncclInt32, ncclSum, static_cast<ncclComm_t>(nccl_comm),
+               static_cast<cudaStream_t>(stream)) != ncclSuccess)
+            return RIDGE_ECOMM;
+    }
     if (M > 0 && ns > 0) {
         // this rank's slab of every rank's C: the same tile coordinates,
         // offset by n0 columns in each buffer
@@ -186,10 +200,8 @@ int ridge_gemm_sharded_p2p(const ridge_tile_config* cfg, const void* A, const vo
                                      ns, K, lda, ldb, ldc, peers, np, stream);
         if (st != RIDGE_OK) return st;
     }
-    if (!nccl_comm || nranks == 1) return RIDGE_OK;
-    AllReduceFn ar = nccl_allreduce();
-    int* word = barrier_word();
-    if (!ar || !word) return RIDGE_ECOMM;
+    if (!fenced) return RIDGE_OK;
+    // Completion barrier: every rank's tiles have landed in this rank's C.
     if (ar(word, word, 1, ncclInt32, ncclSum, static_cast<ncclComm_t>(nccl_comm),
            static_cast<cudaStream_t>(stream)) != ncclSuccess)
         return RIDGE_ECOMM;

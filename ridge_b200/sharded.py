@@ -176,8 +176,12 @@ def sharded_gemm_p2p(a, b_slab, config: TileConfig, peer_c: PeerC, group=None, b
                      stream=None):
     """This rank's slab GEMM with the gather fused into its epilogue: every
     tile lands in every rank's C (peer_c) directly. With barrier=True the call
-    ends with a one-element all-reduce on `stream`, after which this rank's C
-    holds every rank's slab."""
+    is fenced by one-element all-reduces on `stream`: before the kernel (no
+    rank writes into a peer's C until every rank has reached the call, so
+    whatever a rank enqueued on `stream` earlier -- reading its previous C --
+    is done) and after it (this rank's C then holds every rank's slab). A rank
+    that reads its C on the host or on another stream must finish before its
+    next call."""
     M, K = a.shape
     N = peer_c.N
     cc = config.to_c()

@@ -111,3 +111,72 @@ def test_two_rank_fused_p2p_gather_matches_the_nccl_gather():
         p.join(timeout=300)
     results = dict(q.get(timeout=5) for _ in procs)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def _worker_p2p_back_to_back(rank, world, port, q):
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import oracle
+    import ridge_b200 as rb
+    from ridge_b200.sharded import PeerC, sharded_gemm_p2p, slab_bounds
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    try:
+        M, N, K = 768, 2048, 1024
+        cfg = rb.TileConfig(256, 256, 64, 6, 4, 8, 2)
+        rows = np.array([0, 1, 383, 500, M - 1], np.int64)
+        cases = []
+        for seed in (3, 4, 5):
+            a, b = oracle.unit_inputs(M, N, K, seed=seed)
+            n0, ns = slab_bounds(N, world, rank)
+            cases.append((torch.from_numpy(a.view(np.float16)).to(dev),
+                          torch.from_numpy(np.ascontiguousarray(b[n0:n0 + ns]).view(np.float16)).to(dev),
+                          oracle.gemm_f64(a, b, rows=rows)))
+        pc = PeerC(M, N)
+        torch.cuda.synchronize()
+        dist.barrier()
+        # Back-to-back calls, no host barrier between them; rank 1 is slow to
+        # read each result. The entry barrier keeps rank 0's next call from
+        # overwriting rank 1's C before rank 1 has read it.
+        for it in range(6):
+            a_d, b_d, ref = cases[it % 3]
+            full = sharded_gemm_p2p(a_d, b_d, cfg, pc)
+            torch.cuda.synchronize()
+            if rank == 1:
+                time.sleep(0.3)
+            got = full.cpu().numpy().view(np.uint16)[rows]
+            rel, _m, excess = oracle.fp16_stats(got, ref)
+            assert rel <= oracle.REL_FROB_TOL and excess <= oracle.MAX_ABS_EXCESS_TOL, (
+                rank, it, rel, excess)
+        assert rb.device_error() == 0
+        pc.close()
+        q.put((rank, "ok"))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_fused_p2p_back_to_back_calls():
+    """Consecutive ridge_gemm_sharded_p2p calls with different inputs and no
+    host barrier between them, one rank reading each result late: every
+    result each rank reads matches the FP64 oracle on sampled rows."""
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_p2p_back_to_back, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    results = dict(q.get(timeout=5) for _ in procs)
+    assert results == {0: "ok", 1: "ok"}, results

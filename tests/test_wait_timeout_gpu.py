@@ -34,3 +34,29 @@ def test_selftest_rejects_out_of_range_limits():
     code, waited = C.c_int32(), C.c_int64()
     for bad in (0, 999999, 2000000001):
         assert rb.lib.ridge_selftest_wait_timeout(bad, C.byref(code), C.byref(waited)) == -1
+
+
+def test_cleared_error_resets_cached_workspace_counters():
+    """Stale split-K counters in the library's cached workspace (the state a
+    GEMM that gave up can leave) are reset by ridge_device_error(clear): the
+    next split launch through ridge_gemm_launch matches the FP64 oracle."""
+    import numpy as np
+
+    import oracle
+    import ridge_b200 as rb
+    M, N, K = 512, 512, 4096
+    cfg = rb.TileConfig(128, 128, 64, 4, 4, 8)
+    a, b = oracle.unit_inputs(M, N, K, seed=9)
+    ad = torch.from_numpy(a.view(np.float16)).cuda()
+    bd = torch.from_numpy(b.view(np.float16)).cuda()
+    ref = oracle.gemm_f64(a, b)
+    rb.gemm(ad, bd, config=cfg)                  # the stream's workspace exists
+    torch.cuda.synchronize()
+    assert rb.lib.ridge_selftest_stale_counters(3) == 0
+    assert rb.device_error(clear=True) == 7
+    for _ in range(2):
+        c = rb.gemm(ad, bd, config=cfg)
+        torch.cuda.synchronize()
+        assert rb.device_error() == 0
+        rel, _m, excess = oracle.fp16_stats(c.cpu().numpy().view(np.uint16), ref)
+        assert rel <= oracle.REL_FROB_TOL and excess <= oracle.MAX_ABS_EXCESS_TOL, (rel, excess)

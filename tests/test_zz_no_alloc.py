@@ -23,7 +23,7 @@ pytestmark = [pytest.mark.gpu,
 CASES = [
     ((512, 512, 4096), (128, 128, 64, 4, 4, 8)),
     ((2048, 2560, 512), (256, 256, 64, 4, 8, 8, 2)),
-    ((1000, 1000, 1000), (128, 128, 32, 3, 4, 8)),
+    ((1000, 1000, 300), (128, 128, 32, 3, 4, 8)),     # ragged, 2-way split: ~8 MB of scratch
 ]
 
 
@@ -71,3 +71,37 @@ def test_noalloc_rejects_launch_that_needs_more_scratch():
     b = torch.zeros((N, K), dtype=torch.float16, device="cuda")
     c = torch.zeros((M, N), dtype=torch.float16, device="cuda")
     assert _launch_noalloc(rb, cfg, a, b, c, M, N, K) == RIDGE_ENOSCRATCH
+
+
+def test_noalloc_scratch_recovers_after_an_aborted_launch():
+    """A GEMM that gives up mid-launch can leave split-K counters non-zero in
+    the shared scratch, which lives as long as the process. Plant that state on
+    the host (ridge_selftest_stale_counters: no kernel, no fault), show that a
+    split launch then misses its reduction, and that ridge_device_error(clear)
+    restores the scratch so the next launch matches the FP64 oracle."""
+    import ridge_b200 as rb
+    (M, N, K), c = CASES[0]
+    cfg = rb.TileConfig(*c)
+    a, b = oracle.unit_inputs(M, N, K, seed=5)
+    ad = torch.from_numpy(a.view(np.float16)).cuda()
+    bd = torch.from_numpy(b.view(np.float16)).cuda()
+    ref = oracle.gemm_f64(a, b)
+    out = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+    assert _launch_noalloc(rb, cfg, ad, bd, out, M, N, K) == 0   # scratch set up
+    torch.cuda.synchronize()
+    assert rb.device_error() == 0
+
+    assert rb.lib.ridge_selftest_stale_counters(1) == 0
+    out.fill_(float("nan"))
+    assert _launch_noalloc(rb, cfg, ad, bd, out, M, N, K) == 0
+    torch.cuda.synchronize()
+    assert torch.isnan(out.float()).any(), "stale counters should have hidden the split tiles"
+    assert rb.device_error(clear=True) == 7        # the planted code; clearing resets the scratch
+
+    for _ in range(2):
+        out.fill_(float("nan"))
+        assert _launch_noalloc(rb, cfg, ad, bd, out, M, N, K) == 0
+        torch.cuda.synchronize()
+        assert rb.device_error() == 0
+        rel, _max_abs, excess = oracle.fp16_stats(out.cpu().numpy().view(np.uint16), ref)
+        assert rel <= oracle.REL_FROB_TOL and excess <= oracle.MAX_ABS_EXCESS_TOL, (rel, excess)
