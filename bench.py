@@ -2,20 +2,30 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ridge|reference]
 
-One step = one launch of the GEMM (C = A * B, FP16 in, FP32 accumulate, FP16
-out) over one batch of synthetic input: A 4096 x 4096 row-major and this rank's
-4096 x 4096 N-column slab of B (column-major), drawn U(-1,1) from the
-reference's LCG seeded 0 (A first, then B). At N GPUs the GEMM is
-4096 x (4096*N) x 4096, split by N-column slabs of B with A replicated: every
-rank computes one 4096^3 slab, no collective on the data path (weak scaling).
+One step = one pass of the GEMM (C = A * B, FP16 in, FP32 accumulate, FP16
+out) over one batch of synthetic input: BATCH (16) independent problems, each
+A 4096 x 4096 row-major and this rank's 4096 x 4096 N-column slab of B
+(column-major), problem i drawn U(-1,1) from the reference's LCG seeded i (A
+first, then the full B, of which rank r keeps slab r). At N GPUs every rank
+computes its own slabs: no collective on the data path (weak scaling). L2 is
+flushed (256 MiB write) before every launch and only the GEMM sits between the
+CUDA events, so each launch reads A and B from HBM.
 
-value   = whole-job TFLOP/s with inputs resident in HBM: sum over ranks of
-          2*M*N_slab*K per step / (max over ranks of the summed per-step GEMM
-          time). L2 is flushed (256 MiB write) before every timed launch and
-          only the GEMM sits between the CUDA events.
-e2e     = the same metric through the public C ABI with host buffers: each step
-          copies A and the B slab from pinned host memory, launches, and copies
-          C back, all inside the timed region.
+value   = whole-job TFLOP/s with inputs resident in HBM: all ranks' 2*M*N_slab*K
+          per launch x launches / max over ranks of the summed GEMM time of the
+          K timed steps (CUDA events around each launch on its stream).
+          `back_to_back` beside it: the same launches with no flush between
+          them (cold operands, 1.5 GiB cycled), the sustained rate under the
+          1 kW power cap.
+e2e     = the same metric through the public C ABI with host buffers: every
+          problem of every step copies A and the B slab from pinned host memory,
+          launches and copies C back (ridge_gemm_host), all in the timed region.
+c5      = BASELINE config 5 beside the headline: 16384^3 split into N-column
+          slabs over the N ranks, each rank's epilogue storing its tiles into
+          every rank's full C over NVLink (ridge_gemm_sharded_p2p), timed as max
+          over ranks, with the NCCL all-gather variant (ridge_gemm_sharded) and
+          the GEMM alone beside it, and the gathered C checked on every rank
+          against an FP64 product of sampled rows.
 --impl reference  times the reference's own CPU GEMM (referenceGemm, FP64,
           bench/check-gemm.cu:98-108, built from the reference sources into
           oracle/_ref) on all host cores over a row sample of the same workload.
@@ -41,7 +51,9 @@ METRIC = "FP16 GEMM TFLOP/s (4096^3) vs B200 peak"
 UNIT = "TFLOP/s"
 # Best 4096^3 config from the autotuner on B200 (model-pruned, top-k measured).
 BEST_CONFIG = dict(BM=256, BN=256, BK=64, stages=6, warps=4, groupM=8, cta_group=2)
+BATCH = 16          # problems per step, each with its own operands
 L2_FLUSH_BYTES = 256 << 20
+C5_SHAPE = 16384
 
 
 def _peaks():
@@ -264,9 +276,146 @@ def run_reference(args):
     return 0
 
 
-def run_ridge(args):
-    import ctypes as C
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
+
+def _fp16_check(got, ref):
+    """(relative Frobenius error, max |dC| beyond half an FP16 ulp of the FP64
+    value) of an FP16 result against an FP64 reference, on the device; the
+    acceptance bound is 1e-3 and 2e-2 (the test suite's tolerance)."""
+    import torch
+    g = got.double()
+    d = (g - ref).abs()
+    rel = float(d.norm() / ref.norm().clamp_min(1e-300))
+    mag = ref.abs().clamp_min(2.0 ** -14)
+    half_ulp = torch.exp2(torch.floor(torch.log2(mag)) - 11)
+    return rel, float((d - half_ulp).max())
+
+
+def c5_record(cfg, world, rank, dev, steps=3, rounds=3, warmup=1):
+    """BASELINE config 5 on `world` ranks: 16384^3 split into N-column slabs of
+    B with A replicated, C gathered on every rank. Returns the sub-record."""
+    import torch
+    import torch.distributed as dist
+
+    import ridge_b200 as rb
+    from ridge_b200.sharded import PeerC, sharded_gemm, sharded_gemm_p2p, slab_bounds, slab_gemm
+
+    M = N = K = C5_SHAPE
+    n0, ns = slab_bounds(N, world, rank)
+    a = torch.empty((M, K), dtype=torch.float16, device=dev)
+    st_b = rb.fill_lcg(a, 0)
+    b_slab = torch.empty((max(ns, 1), K), dtype=torch.float16, device=dev)[:ns]
+    if ns:
+        rb.fill_lcg(b_slab, rb.lcg_advance(st_b, n0 * K))
+    pc = PeerC(M, N) if world > 1 else None
+    c_full = pc.local if pc is not None else torch.empty((M, N), dtype=torch.float16, device=dev)
+    c_slab = torch.empty((M, max(ns, 1)), dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def gemm_alone():
+        slab_gemm(a, b_slab, c_slab, cfg)
+
+    def fused():
+        if pc is not None:
+            sharded_gemm_p2p(a, b_slab, cfg, pc)
+        else:
+            slab_gemm(a, b_slab, c_full, cfg)   # one rank: its slab is all of C
+
+    b_slab.full_n = N
+    nccl_out = {}
+
+    def nccl_gather():
+        nccl_out["c"] = sharded_gemm(a, b_slab, cfg, gather=True, rank=rank, world=world)[1]
+
+    # The 16384^3 GEMM runs into the 1 kW power cap within milliseconds:
+    # under continuous load one launch slows from ~5.9 to ~7.9 ms over ~100 ms,
+    # so a variant timed after another would look slower. Each variant's block
+    # therefore starts after a pause that lets the clock recover, the order
+    # rotates every round, each launch has its own events, and per variant the
+    # median launch counts (then the max over ranks).
+    variants = {"gemm": gemm_alone, "nccl": nccl_gather, "fused": fused}
+    times = {k: [] for k in variants}
+    c_full.fill_(float("nan"))
+    for _ in range(warmup):
+        for fn in variants.values():
+            fn()
+    torch.cuda.synchronize()
+    names = list(variants)
+    for r in range(rounds):
+        for name in names[r % len(names):] + names[:r % len(names)]:
+            fn = variants[name]
+            time.sleep(0.25)
+            if world > 1:
+                dist.barrier()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(steps)]
+            for e0, e1 in evs:
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            times[name] += [e0.elapsed_time(e1) for e0, e1 in evs]
+    med = {k: _max_over_ranks(statistics.median(v), world, dev) for k, v in times.items()}
+    gemm_ms, nccl_ms, fused_ms = med["gemm"], med["nccl"], med["fused"]
+    if rb.device_error() != 0:
+        raise RuntimeError("device error in the 16384^3 sharded GEMM")
+
+    # Every rank checks its gathered C: 16 sampled rows (first, last, middle,
+    # seeded random) against an FP64 product over all N columns, B regenerated
+    # in 2048-row chunks from the same LCG stream.
+    g = torch.Generator().manual_seed(7)
+    rows = sorted({0, 1, M // 2, M - 1, *torch.randint(0, M, (12,), generator=g).tolist()})
+    rows_t = torch.tensor(rows, device=dev)
+    a_rows = a.index_select(0, rows_t).double()
+    ref = torch.empty((len(rows), N), dtype=torch.float64, device=dev)
+    chunk = torch.empty((2048, K), dtype=torch.float16, device=dev)
+    for c0 in range(0, N, 2048):
+        rb.fill_lcg(chunk, rb.lcg_advance(st_b, c0 * K))
+        ref[:, c0:c0 + 2048] = a_rows @ chunk.double().t()
+    got = c_full.index_select(0, rows_t)
+    rel, excess = _fp16_check(got, ref)
+    same_as_nccl = bool(torch.equal(got, nccl_out["c"].index_select(0, rows_t)))
+    ok = rel <= 1e-3 and excess <= 2e-2
+    oks = _max_over_ranks(0.0 if ok else 1.0, world, dev) == 0.0
+    rel = _max_over_ranks(rel, world, dev)
+    same = _max_over_ranks(0.0 if same_as_nccl else 1.0, world, dev) == 0.0
+    if pc is not None:
+        pc.close()
+
+    peak, _hbm, peak_src = _peaks()
+    flops = 2.0 * M * N * K
+    peer_bytes = float(M) * ns * 2 * (world - 1)      # this rank's tiles to the other ranks
+    rec = {
+        "workload": "%dx%dx%d FP16 GEMM in %d N-slab(s) of %d columns, A replicated, full C "
+                    "gathered on every rank" % (M, N, K, world, ns),
+        "tile": cfg.as_dict(), "launches_per_variant": steps * rounds, "warmup": warmup,
+        "ms_fused_gather": fused_ms, "tflops_fused_gather": flops / (fused_ms * 1e-3) / 1e12,
+        "frac_of_n_peak": flops / (fused_ms * 1e-3) / 1e12 / (world * peak),
+        "peak_source": peak_src + " bf16 dense (burst), per GPU",
+        "ms_gemm_alone": gemm_ms, "tflops_gemm_alone": flops / (gemm_ms * 1e-3) / 1e12,
+        "ms_nccl_gather": nccl_ms, "tflops_nccl_gather": flops / (nccl_ms * 1e-3) / 1e12,
+        "peer_store_gbs_per_rank": (peer_bytes / (fused_ms * 1e-3) / 1e9) if world > 1 else 0.0,
+        "limiter": ("GEMM (tensor pipe)" if fused_ms <= 1.03 * gemm_ms else
+                    "epilogue peer stores over NVLink (%.0f GB/s per rank)"
+                    % (peer_bytes / (fused_ms * 1e-3) / 1e9)),
+        "check": {"rows_per_rank": len(rows), "rel_frob_max_over_ranks": rel,
+                  "passed_on_every_rank": oks, "fused_equals_nccl_gather": same,
+                  "reference": "FP64 product of the sampled rows (torch float64 on the device)"},
+        "timing": "CUDA events around each launch; variant blocks after a 0.25 s pause, order "
+                  "rotated every round; median launch per variant, max over ranks; operands > L2",
+    }
+    return rec
+
+
+def run_ridge(args):
     import torch
     import torch.distributed as dist
 
@@ -281,20 +430,16 @@ def run_ridge(args):
     cfg = rb.TileConfig(**BEST_CONFIG)
     if args.config:
         cfg = rb.TileConfig(*[int(x) for x in args.config.split(",")])
-    # Inputs: one LCG stream from seed 0: A, then the full B (N x K storage);
-    # each rank keeps its N-slab (rows [rank*N_SLAB, (rank+1)*N_SLAB) of B).
-    a = torch.empty((M, K), dtype=torch.float16, device=dev)
-    st = rb.fill_lcg(a, 0)
-    b = torch.empty((N_SLAB, K), dtype=torch.float16, device=dev)
-    if rank > 0:
-        # advance the stream past the earlier ranks' slabs
-        skip = torch.empty((N_SLAB, K), dtype=torch.float16, device=dev)
-        for _ in range(rank):
-            st = rb.fill_lcg(skip, st)
-        del skip
-    rb.fill_lcg(b, st)
-    c = torch.empty((M, N_SLAB), dtype=torch.float16, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    # Problem i: A then the full B (N_SLAB * world rows of K) from the LCG
+    # seeded i; this rank keeps B rows [rank * N_SLAB, (rank + 1) * N_SLAB).
+    probs = []
+    for i in range(BATCH):
+        a = torch.empty((M, K), dtype=torch.float16, device=dev)
+        st = rb.fill_lcg(a, i)
+        b = torch.empty((N_SLAB, K), dtype=torch.float16, device=dev)
+        rb.fill_lcg(b, rb.lcg_advance(st, rank * N_SLAB * K))
+        c = torch.empty((M, N_SLAB), dtype=torch.float16, device=dev)
+        probs.append((a, b, c))
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
 
@@ -304,48 +449,73 @@ def run_ridge(args):
         if s != 0:
             raise rb.RidgeError(s, "ridge_gemm_launch")
 
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     for _ in range(args.warmup):
-        flush.zero_()
-        launch(a, b, c)
+        for p in probs:
+            flush.zero_()
+            launch(*p)
     torch.cuda.synchronize()
     if rb.device_error() != 0:
         raise RuntimeError("device error during warm-up")
 
     # ------------------------------------------------ device-resident timing
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    n_launch = args.steps * BATCH
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(n_launch)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(n_launch)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        for i in range(args.steps):
+        for i in range(n_launch):
             flush.zero_()
-            starts[i].record(stream)
-            launch(a, b, c)
-            ends[i].record(stream)
+            ev0[i].record(stream)
+            launch(*probs[i % BATCH])
+            ev1[i].record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(per_step)
+    per_launch = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
+    total_ms = _max_over_ranks(sum(per_launch), world, dev)
+    flops_launch = 2.0 * M * N_SLAB * K
+    value = world * flops_launch * n_launch / (total_ms * 1e-3) / 1e12
+    kernel_ms = sum(per_launch) / n_launch
+    per_step_tf = sorted(flops_launch * BATCH / (sum(per_launch[s * BATCH:(s + 1) * BATCH]) * 1e-3)
+                         / 1e12 for s in range(args.steps))
+    del flush
+
+    # the same launches back to back (no flush): the sustained rate
     if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    flops_step = 2.0 * M * N_SLAB * K
-    value = world * flops_step * args.steps / (total_ms * 1e-3) / 1e12
-    kernel_ms = total_ms / args.steps
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks_b2b:
+        e0.record(stream)
+        for i in range(n_launch):
+            launch(*probs[i % BATCH])
+        e1.record(stream)
+        torch.cuda.synchronize()
+    b2b_ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    b2b_value = world * flops_launch * n_launch / (b2b_ms * 1e-3) / 1e12
     if rb.device_error() != 0:
         raise RuntimeError("device error during the timed region")
+    # spot check of the timed kernel's output: problem 0's C against an FP64
+    # product of sampled rows (torch float64 on the device)
+    a0, b0, c0 = probs[0]
+    rows_t = torch.tensor([0, 1, 2047, M - 1], device=dev)
+    ref0 = a0.index_select(0, rows_t).double() @ b0.double().t()
+    rel0, exc0 = _fp16_check(c0.index_select(0, rows_t), ref0)
+    timed_ok = rel0 <= 1e-3 and exc0 <= 2e-2
 
     # ------------------------------------------------ end to end (host buffers)
     # The user-facing host-buffer call, ridge_gemm_host: page-locked A and B in,
     # C out, the copies pipelined against the kernel by M-panels inside the call.
+    import ctypes as C
     a_h = torch.empty((M, K), dtype=torch.float16).pin_memory()
     b_h = torch.empty((N_SLAB, K), dtype=torch.float16).pin_memory()
     c_h = torch.empty((M, N_SLAB), dtype=torch.float16).pin_memory()
-    a_h.copy_(a)
-    b_h.copy_(b)
+    a_h.copy_(a0)
+    b_h.copy_(b0)
     cc = cfg.to_c()
 
     def host_call():
@@ -362,25 +532,25 @@ def run_ridge(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(args.steps * BATCH):
         host_call()
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * flops_step * args.steps / (e2e_ms * 1e-3) / 1e12
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world, dev)
+    e2e_value = world * flops_launch * args.steps * BATCH / (e2e_ms * 1e-3) / 1e12
     # Same kernel, but panels change the split-K tail plan (summation order):
     # agreement to FP16 rounding, not bit for bit.
-    cr = c.float().cpu()
+    cr = c0.float().cpu()
     ok = bool(((c_h.float() - cr).norm() / cr.norm()).item() <= 1e-3)
+
+    c5 = None
+    if not args.no_c5:
+        c5 = c5_record(cfg, world, rank, dev)
 
     # ------------------------------------------------ report (rank 0)
     if rank == 0:
         peak, _hbm, peak_src = _peaks()
-        achieved = flops_step / (kernel_ms * 1e-3) / 1e12
+        achieved = flops_launch / (kernel_ms * 1e-3) / 1e12
         workload = "4096x4096x4096 slab"
         traffic = _traffic(workload)
         cpu = None
@@ -392,27 +562,41 @@ def run_ridge(args):
                    "kind": ref.kind, "sample": ref.sample_text(rows, dt)}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": kernel_ms,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic: reference LCG mapped to U(-1,1), seed 0, A then B (device fill)",
+            "data": "synthetic: reference LCG mapped to U(-1,1), problem i seeded i, A then B "
+                    "(device fill)",
             "config": {
-                "workload": "%dx%dx%d FP16 GEMM per rank (N-slab of %dx%dx%d, A replicated)"
-                            % (M, N_SLAB, K, M, N_SLAB * world, K),
+                "workload": "%d x (%dx%dx%d FP16 GEMM) per rank per step (N-slab of %dx%dx%d, "
+                            "A replicated)" % (BATCH, M, N_SLAB, K, M, N_SLAB * world, K),
                 "tile": cfg.as_dict(), "layout": "A row-major, B column-major, C row-major FP16",
                 "accumulate": "fp32", "parallelism": "n-slab x%d" % world,
-                "l2": "flushed before every timed launch (256 MiB write), inputs 96 MiB < L2",
-                "timing": "CUDA events around each launch, summed; max over ranks",
+                "l2": "flushed before every timed launch (256 MiB write); %d problems with their "
+                      "own operands (%.2f GiB)" % (BATCH, BATCH * 3 * M * K * 2 / 2 ** 30),
+                "timing": "CUDA events around each launch on the launching stream, summed; "
+                          "max over ranks",
             },
+            "back_to_back": {"value": b2b_value, "unit": UNIT,
+                             "ms_per_launch": b2b_ms / n_launch,
+                             "how": "the same %d launches with no flush between them (operands "
+                                    "cycled, cold in L2), one event pair around all; the rate "
+                                    "the 1 kW power cap sustains" % n_launch,
+                             "clocks": clocks_b2b.summary()},
+            "per_step_tflops": {"min": per_step_tf[0],
+                                "median": per_step_tf[len(per_step_tf) // 2],
+                                "max": per_step_tf[-1]},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": peak_src + " bf16 dense (burst)",
                          "traffic": traffic},
             "clocks": clocks.summary(),
             "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": (M * K + N_SLAB * K) * 2,
-                    "d2h_bytes_per_step": M * N_SLAB * 2},
-            "gpu_launches": args.steps,
+                    "h2d_bytes_per_step": BATCH * (M * K + N_SLAB * K) * 2,
+                    "d2h_bytes_per_step": BATCH * M * N_SLAB * 2},
+            "gpu_launches": n_launch,
+            "timed_result_check": {"rows": 4, "rel_frob": rel0, "passed": timed_ok},
             "e2e_result_matches": ok,
+            "c5": c5,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -424,10 +608,11 @@ def run_ridge(args):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ridge", "reference"], default="ridge")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c5", action="store_true", help="skip the 16384^3 sharded sub-record")
     ap.add_argument("--panels", type=int, default=0,
                     help="M-panels of the end-to-end host-buffer call (0 = its default)")
     ap.add_argument("--config", default=None,

@@ -10,11 +10,11 @@ raises ImportError -- there is no CPU fallback.
 
 from ._native import RidgeError, exported_symbols, lib  # noqa: F401
 from .gemm import (DEFAULT_CONFIG, TileConfig, VariantInfo, config_info, config_ok,  # noqa: F401
-                   device_error, fill_lcg, gemm, gemm_host, launch_raw, synthetic_inputs, num_variants, valid_for_shape, variant,
+                   device_error, fill_lcg, gemm, gemm_host, launch_raw, lcg_advance, synthetic_inputs, num_variants, valid_for_shape, variant,
                    variants)
 
 __all__ = [
     "RidgeError", "TileConfig", "VariantInfo", "DEFAULT_CONFIG", "gemm", "gemm_host", "launch_raw",
     "variants", "variant", "num_variants", "config_info", "config_ok", "valid_for_shape",
-    "device_error", "exported_symbols", "lib", "fill_lcg", "synthetic_inputs",
+    "device_error", "exported_symbols", "lib", "fill_lcg", "lcg_advance", "synthetic_inputs",
 ]

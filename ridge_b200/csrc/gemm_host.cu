@@ -607,8 +607,10 @@ int ridge_config_valid_for_shape(const ridge_tile_config* cfg, int64_t M, int64_
 int ridge_gemm_workspace_size(const ridge_tile_config* cfg, int64_t M, int64_t N, int64_t K,
                               int64_t* bytes) {
     if (!bytes) return RIDGE_EINVAL;
-    int st = ridge_config_valid_for_shape(cfg, M, N, K, std::max<int64_t>(K, 8),
-                                          std::max<int64_t>(K, 8), N);
+    // The workspace does not depend on the pitches: validate with the
+    // smallest legal ones (K rounded up to a multiple of 8).
+    const int64_t ld = (std::max<int64_t>(K, 8) + 7) / 8 * 8;
+    int st = ridge_config_valid_for_shape(cfg, M, N, K, ld, ld, N);
     if (st != RIDGE_OK) return st;
     *bytes = 0;
     if (M == 0 || N == 0 || K == 0) return RIDGE_OK;

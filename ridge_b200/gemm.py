@@ -193,6 +193,20 @@ def fill_lcg(out, seed_state: int = 0, unit: bool = True, stream=None) -> int:
     return st.value
 
 
+def lcg_advance(state: int, n: int) -> int:
+    """The LCG state after n more draws from `state` (s -> 1664525 s +
+    1013904223 mod 2^32, applied n times by repeated squaring of the affine
+    map), so a rank can start its slab of B without drawing the rows before it."""
+    a, c = 1664525, 1013904223
+    ra, rc = 1, 0                      # the identity map
+    while n > 0:
+        if n & 1:
+            ra, rc = (a * ra) & 0xFFFFFFFF, (a * rc + c) & 0xFFFFFFFF
+        a, c = (a * a) & 0xFFFFFFFF, (a * c + c) & 0xFFFFFFFF
+        n >>= 1
+    return (ra * state + rc) & 0xFFFFFFFF
+
+
 def synthetic_inputs(M: int, N: int, K: int, seed: int = 0, device=None):
     """The benchmark operands: A (M, K) then B (N, K) drawn U(-1, 1) from one
     LCG stream seeded `seed` (B is the N x K storage of a column-major B)."""
