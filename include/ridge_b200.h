@@ -41,8 +41,10 @@ const char* ridge_status_string(int status);
  * ridge::GemmConfig (include/ridge/config.h:18-39) and the fields of
  * ridgebench::KernelVariant (bench/kernels/gemm-mma.cuh:368-383).
  *   BM, BN   output tile (64, 128 or 256 each)
- *   BK       K depth of one pipeline stage (32 or 64 FP16 = one 64B/128B swizzle row)
- *   stages   shared-memory ring depth (2..8)
+ *   BK       K depth of one pipeline stage: 32 or 64 FP16 (one 64B / 128B swizzle
+ *            row) or 128 (two 128B-swizzled K atoms per TMA box; K a multiple of 64)
+ *   stages   shared-memory ring depth: 2..8 accepted by ridge_config_check (where
+ *            shared memory allows); the registered table holds 2..6
  *   warps    epilogue warps draining TMEM (4 or 8); the CTA adds one TMA
  *            producer warp and one MMA-issuer warp
  *   groupM   grouped-M launch order width (gemm-mma.cuh:158-178); 1 = row-major

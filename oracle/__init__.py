@@ -31,12 +31,14 @@ _i64 = C.c_int64
 
 def build(reference: str | None = None) -> None:
     """Builds libridge_oracle.so, and _ref/libridge_ref.so when the reference
-    sources exist at `reference` (default /root/reference)."""
+    sources are found at `reference` or, if that is not given, at the path in
+    the RIDGE_REFERENCE environment variable (no default location)."""
     targets = ["liboracle"]
-    ref = reference or os.environ.get("RIDGE_REFERENCE", "/root/reference")
-    if Path(ref, "bench", "check-gemm.cu").exists():
+    ref = reference or os.environ.get("RIDGE_REFERENCE", "")
+    if ref and Path(ref, "bench", "check-gemm.cu").exists():
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), "REF=%s" % ref, *targets], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE)] + (["REF=%s" % ref] if ref else []) + targets,
+                   check=True)
 
 
 def _load():

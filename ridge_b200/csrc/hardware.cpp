@@ -99,7 +99,8 @@ bool parse_flat_json(const std::string& s, std::map<std::string, std::string>& k
             continue;
         }
         if (i < s.size() && s[i] == '}') return true;
-        err = "expected ',' or '}' at offset " + std::to_string(i);
+        err = "value of \"" + key + "\" is followed by neither a comma nor the closing brace "
+              "(byte " + std::to_string(i) + ")";
         return false;
     }
 }
@@ -108,7 +109,7 @@ bool number(const std::map<std::string, std::string>& kv, const char* key, doubl
             std::string& err) {
     auto it = kv.find(key);
     if (it == kv.end()) {
-        err = std::string("missing required key \"") + key + "\"";
+        err = std::string("constant \"") + key + "\" is absent (every constant is required)";
         return false;
     }
     char* end = nullptr;

@@ -1,201 +1,346 @@
-// ridge-predict: the B200 cost model from the command line.
+// ridge-predict: command-line front end of the B200 cost model (ridge_predict
+// in libridge_b200).
 //
-// Same interface as the reference CLI (tools/ridge-predict.cpp:15-168): single
-// prediction from flags, or --batch in.csv --out out.csv, which copies every
-// row (and `#` comment line) and appends the prediction columns, matching input
-// columns by name so a measured sweep can be fed straight in. Python tools get
-// their predictions here or through ridge_predict in the library -- one copy of
-// the math.
+// Drop-in contract with the reference tool (tools/ridge-predict.cpp there):
+//   * the flags --gpu, --hw, --m/--n/--k, --bm/--bn/--bk, --stages, --batch,
+//     --out; the sm_80 warp-tile flags --warpm/--warpn/--regs are accepted and
+//     have no effect (tcgen05 tiles have no warp tile);
+//   * --batch IN --out OUT joins by column name: every input line is copied
+//     (comment lines starting with '#' too) and each data row gets the eight
+//     pred_* columns, so a measured sweep can be fed in as it is.
+// This build adds --warps, --groupm, --cta-group, --split-k (and the CSV
+// columns warps, groupM, cta_group, split_k, defaulted when absent so older
+// CSVs still load) and --json for a machine-readable single prediction.
 //
-// Kept from the reference: --gpu / --hw / --m --n --k / --bm --bn --bk /
-// --stages / --batch / --out and the eight pred_* columns. The sm_80 warp-tile
-// flags (--warpm --warpn --regs) are accepted and ignored (tcgen05 has no warp
-// tile). New: --warps --groupm --cta-group --split-k, and the input columns
-// warps, groupM, cta_group, split_k (defaults when absent, so reference CSVs
-// still parse).
+// Structure: a table of option descriptors drives the parser (each names the
+// field it sets), a ColumnMap resolves CSV header names to indices once, and
+// the single-prediction report is rendered from a list of labelled values.
 
+#include <cerrno>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <fstream>
-#include <sstream>
+#include <memory>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/ridge_b200.h"
 
 namespace {
 
-void usage() {
-    std::printf(
-        "ridge-predict: predict B200 FP16 tcgen05 GEMM throughput and bottleneck.\n"
-        "Usage:\n"
-        "  ridge-predict [--gpu b200 | --hw model.json]\n"
-        "                [--m M --n N --k K]\n"
-        "                [--bm BM --bn BN --bk BK --stages S --warps W --groupm G]\n"
-        "                [--cta-group 0|1|2 --split-k 0|1]\n"
-        "                [--batch in.csv --out out.csv]\n"
-        "Defaults: built-in B200 placeholders, 4096^3, 128x256x64 tile, 4 stages,\n"
-        "4 epilogue warps, groupM 8.\n");
+struct Options {
+    ridge_gemm_config cfg{};
+    std::string gpu = "b200";
+    std::string hw_json;
+    std::string batch_in;
+    std::string batch_out = "predictions.csv";
+    bool json = false;
+    bool help = false;
+};
+
+enum class Kind { I64, I32, Text, Flag, Ignored };
+
+struct OptionSpec {
+    const char* flag;
+    Kind kind;
+    void* target;  // int64_t*, int32_t*, std::string* or bool*; unused for Ignored
+};
+
+std::vector<OptionSpec> option_table(Options& o) {
+    return {
+        {"--gpu", Kind::Text, &o.gpu},          {"--hw", Kind::Text, &o.hw_json},
+        {"--batch", Kind::Text, &o.batch_in},   {"--out", Kind::Text, &o.batch_out},
+        {"--m", Kind::I64, &o.cfg.M},           {"--n", Kind::I64, &o.cfg.N},
+        {"--k", Kind::I64, &o.cfg.K},           {"--bm", Kind::I32, &o.cfg.tile.BM},
+        {"--bn", Kind::I32, &o.cfg.tile.BN},    {"--bk", Kind::I32, &o.cfg.tile.BK},
+        {"--stages", Kind::I32, &o.cfg.tile.stages},
+        {"--warps", Kind::I32, &o.cfg.tile.warps},
+        {"--groupm", Kind::I32, &o.cfg.tile.groupM},
+        {"--cta-group", Kind::I32, &o.cfg.tile.cta_group},
+        {"--split-k", Kind::I32, &o.cfg.tile.split_k},
+        {"--json", Kind::Flag, &o.json},        {"--help", Kind::Flag, &o.help},
+        {"-h", Kind::Flag, &o.help},            {"--warpm", Kind::Ignored, nullptr},
+        {"--warpn", Kind::Ignored, nullptr},    {"--regs", Kind::Ignored, nullptr},
+    };
 }
 
-std::vector<std::string> split_csv(const std::string& line) {
-    std::vector<std::string> cells;
-    std::string cell;
-    std::istringstream ss(line);
-    while (std::getline(ss, cell, ',')) cells.push_back(cell);
-    return cells;
+const char* kHelp =
+    "ridge-predict -- B200 (sm_100a) tcgen05 FP16 GEMM cost model\n"
+    "\n"
+    "  one prediction:  ridge-predict [--m M --n N --k K] [tile flags] [--json]\n"
+    "  CSV join:        ridge-predict --batch sweep.csv [--out predictions.csv]\n"
+    "\n"
+    "  hardware   --gpu b200 (built-in constants) | --hw constants.json\n"
+    "  tile       --bm --bn --bk --stages --warps --groupm --cta-group 0|1|2 --split-k 0|1\n"
+    "             (--warpm/--warpn/--regs are accepted for old scripts and ignored)\n"
+    "  defaults   M = N = K = 4096, 128x256x64 tile, 4 stages, 4 epilogue warps, groupM 8\n";
+
+bool parse_int(const char* text, int64_t* out) {
+    if (!text || !*text) return false;
+    errno = 0;
+    char* end = nullptr;
+    const long long v = std::strtoll(text, &end, 10);
+    if (errno != 0 || *end != '\0') return false;
+    *out = v;
+    return true;
 }
 
-int run_batch(const std::string& in_path, const std::string& out_path, const ridge_hw& hw,
-              const ridge_gemm_config& defaults) {
-    std::ifstream in(in_path);
+// Accepts "--flag value" and "--flag=value". Returns false (message printed)
+// on an unknown flag, a missing value or a value that is not an integer.
+bool parse_args(int argc, char** argv, Options& o) {
+    const std::vector<OptionSpec> table = option_table(o);
+    for (int i = 1; i < argc; ++i) {
+        std::string arg = argv[i];
+        std::string inline_value;
+        bool has_inline = false;
+        const size_t eq = arg.find('=');
+        if (arg.rfind("--", 0) == 0 && eq != std::string::npos) {
+            inline_value = arg.substr(eq + 1);
+            arg.resize(eq);
+            has_inline = true;
+        }
+        const OptionSpec* spec = nullptr;
+        for (const OptionSpec& s : table)
+            if (arg == s.flag) spec = &s;
+        if (!spec) {
+            std::fprintf(stderr, "ridge-predict: no such option '%s' (try --help)\n", argv[i]);
+            return false;
+        }
+        if (spec->kind == Kind::Flag) {
+            *static_cast<bool*>(spec->target) = true;
+            continue;
+        }
+        const char* value = nullptr;
+        if (has_inline) {
+            value = inline_value.c_str();
+        } else if (i + 1 < argc) {
+            value = argv[++i];
+        } else {
+            std::fprintf(stderr, "ridge-predict: option '%s' needs a value\n", spec->flag);
+            return false;
+        }
+        int64_t n = 0;
+        switch (spec->kind) {
+            case Kind::Text: *static_cast<std::string*>(spec->target) = value; break;
+            case Kind::Ignored: break;
+            case Kind::I64:
+            case Kind::I32:
+                if (!parse_int(value, &n)) {
+                    std::fprintf(stderr, "ridge-predict: '%s' wants an integer, got '%s'\n",
+                                 spec->flag, value);
+                    return false;
+                }
+                if (spec->kind == Kind::I64)
+                    *static_cast<int64_t*>(spec->target) = n;
+                else
+                    *static_cast<int32_t*>(spec->target) = int32_t(n);
+                break;
+            case Kind::Flag: break;
+        }
+    }
+    return true;
+}
+
+bool load_hardware(const Options& o, ridge_hw* hw) {
+    if (!o.hw_json.empty()) {
+        char err[512] = {0};
+        if (ridge_hw_load_json(o.hw_json.c_str(), hw, err, int(sizeof(err))) != RIDGE_OK) {
+            std::fprintf(stderr, "ridge-predict: hardware constants not loaded: %s\n", err);
+            return false;
+        }
+        return true;
+    }
+    if (o.gpu == "b200" || o.gpu == "B200") return ridge_hw_b200(hw) == RIDGE_OK;
+    std::fprintf(stderr, "ridge-predict: no built-in constants for '%s' (only b200; use --hw)\n",
+                 o.gpu.c_str());
+    return false;
+}
+
+// ---------------------------------------------------------------- CSV join
+
+std::vector<std::string> split_fields(const std::string& line) {
+    std::vector<std::string> f;
+    size_t start = 0;
+    for (;;) {
+        const size_t comma = line.find(',', start);
+        f.push_back(line.substr(start, comma == std::string::npos ? std::string::npos
+                                                                  : comma - start));
+        if (comma == std::string::npos) return f;
+        start = comma + 1;
+    }
+}
+
+// Header name -> column index, resolved once per file.
+class ColumnMap {
+  public:
+    explicit ColumnMap(const std::vector<std::string>& header) {
+        for (size_t i = 0; i < header.size(); ++i) index_.emplace(header[i], i);
+    }
+    // Stores the integer in column `name` of `row` into *field; a file without
+    // that column leaves *field at its default. A malformed cell is an error.
+    template <typename T>
+    bool get(const std::vector<std::string>& row, const char* name, T* field) const {
+        const auto it = index_.find(name);
+        if (it == index_.end() || it->second >= row.size()) return true;  // keep the default
+        int64_t v = 0;
+        if (!parse_int(row[it->second].c_str(), &v)) return false;
+        *field = T(v);
+        return true;
+    }
+
+  private:
+    std::unordered_map<std::string, size_t> index_;
+};
+
+constexpr const char* kPredColumns =
+    "pred_tflops,pred_bottleneck,pred_compute_ceiling,pred_hbm_ceiling,pred_smem_eff,"
+    "pred_occ_factor,pred_arith_intensity,pred_ctas_per_sm";
+
+int join_csv(const Options& o, const ridge_hw& hw) {
+    std::ifstream in(o.batch_in);
     if (!in) {
-        std::fprintf(stderr, "cannot open %s\n", in_path.c_str());
+        std::fprintf(stderr, "ridge-predict: cannot read '%s'\n", o.batch_in.c_str());
         return 1;
     }
-    std::ofstream out(out_path);
+    std::FILE* out = std::fopen(o.batch_out.c_str(), "w");
     if (!out) {
-        std::fprintf(stderr, "cannot write %s\n", out_path.c_str());
+        std::fprintf(stderr, "ridge-predict: cannot create '%s'\n", o.batch_out.c_str());
         return 1;
     }
+    std::unique_ptr<ColumnMap> columns;
     std::string line;
-    std::vector<std::string> header;
-    bool have_header = false;
-    int rows = 0;
-    while (std::getline(in, line)) {
+    long line_no = 0, predicted = 0;
+    int status = 0;
+    while (status == 0 && std::getline(in, line)) {
+        ++line_no;
         if (!line.empty() && line.back() == '\r') line.pop_back();
         if (line.empty()) continue;
-        if (line[0] == '#') {
-            out << line << "\n";
+        if (line[0] == '#') {  // comments travel with the data
+            std::fprintf(out, "%s\n", line.c_str());
             continue;
         }
-        const std::vector<std::string> cells = split_csv(line);
-        if (!have_header) {
-            header = cells;
-            have_header = true;
-            out << line
-                << ",pred_tflops,pred_bottleneck,pred_compute_ceiling,pred_hbm_ceiling,"
-                   "pred_smem_eff,pred_occ_factor,pred_arith_intensity,pred_ctas_per_sm\n";
+        const std::vector<std::string> fields = split_fields(line);
+        if (!columns) {
+            columns.reset(new ColumnMap(fields));
+            std::fprintf(out, "%s,%s\n", line.c_str(), kPredColumns);
             continue;
         }
-        auto col = [&](const char* name, long long def) -> long long {
-            for (size_t i = 0; i < header.size() && i < cells.size(); ++i)
-                if (header[i] == name) return std::atoll(cells[i].c_str());
-            return def;
-        };
-        ridge_gemm_config g = defaults;
-        g.M = col("M", g.M);
-        g.N = col("N", g.N);
-        g.K = col("K", g.K);
-        g.tile.BM = int(col("BM", g.tile.BM));
-        g.tile.BN = int(col("BN", g.tile.BN));
-        g.tile.BK = int(col("BK", g.tile.BK));
-        g.tile.stages = int(col("stages", g.tile.stages));
-        g.tile.warps = int(col("warps", g.tile.warps));
-        g.tile.groupM = int(col("groupM", g.tile.groupM));
-        g.tile.cta_group = int(col("cta_group", g.tile.cta_group));
-        g.tile.split_k = int(col("split_k", g.tile.split_k));
+        ridge_gemm_config g = o.cfg;
+        ridge_tile_config& t = g.tile;
+        const bool ok = columns->get(fields, "M", &g.M) && columns->get(fields, "N", &g.N) &&
+                        columns->get(fields, "K", &g.K) && columns->get(fields, "BM", &t.BM) &&
+                        columns->get(fields, "BN", &t.BN) && columns->get(fields, "BK", &t.BK) &&
+                        columns->get(fields, "stages", &t.stages) &&
+                        columns->get(fields, "warps", &t.warps) &&
+                        columns->get(fields, "groupM", &t.groupM) &&
+                        columns->get(fields, "cta_group", &t.cta_group) &&
+                        columns->get(fields, "split_k", &t.split_k);
         ridge_prediction p;
-        if (ridge_predict(&g, &hw, &p) != RIDGE_OK) {
-            std::fprintf(stderr, "%s: row %d: invalid shape\n", in_path.c_str(), rows + 1);
-            return 1;
+        if (!ok || ridge_predict(&g, &hw, &p) != RIDGE_OK) {
+            std::fprintf(stderr, "ridge-predict: %s line %ld: %s\n", o.batch_in.c_str(), line_no,
+                         ok ? "shape or tile the model refuses" : "non-integer value");
+            status = 1;
+            break;
         }
-        out << line << ',' << p.predicted_tflops << ',' << ridge_bottleneck_string(p.bottleneck)
-            << ',' << p.compute_tflops << ',' << p.hbm_tflops << ',' << p.smem_efficiency << ','
-            << p.occ_factor << ',' << p.arithmetic_intensity << ',' << p.ctas_per_sm << '\n';
-        ++rows;
+        std::fprintf(out, "%s,%.9g,%s,%.9g,%.9g,%.9g,%.9g,%.9g,%d\n", line.c_str(),
+                     p.predicted_tflops, ridge_bottleneck_string(p.bottleneck), p.compute_tflops,
+                     p.hbm_tflops, p.smem_efficiency, p.occ_factor, p.arithmetic_intensity,
+                     p.ctas_per_sm);
+        ++predicted;
     }
-    std::fprintf(stderr, "predicted %d rows -> %s (%s constants)\n", rows, out_path.c_str(),
-                 hw.calibrated ? "calibrated" : "placeholder");
+    std::fclose(out);
+    if (status == 0)
+        std::fprintf(stderr, "ridge-predict: %ld row(s) joined into %s [%s hardware constants]\n",
+                     predicted, o.batch_out.c_str(), hw.calibrated ? "measured" : "built-in");
+    return status;
+}
+
+// ---------------------------------------------------------------- one prediction
+
+struct Item {
+    const char* key;
+    double value;
+    const char* unit;
+};
+
+int report_one(const Options& o, const ridge_hw& hw) {
+    const ridge_gemm_config& g = o.cfg;
+    ridge_prediction p;
+    if (ridge_predict(&g, &hw, &p) != RIDGE_OK) {
+        std::fprintf(stderr, "ridge-predict: the model refuses this shape or tile\n");
+        return 1;
+    }
+    const bool fits = p.bottleneck != RIDGE_BOTTLENECK_DOES_NOT_FIT;
+    const char* limiter = ridge_bottleneck_string(p.bottleneck);
+    const std::vector<Item> items = {
+        {"tflops", p.predicted_tflops, "TFLOP/s"},
+        {"compute_ceiling", p.compute_tflops, "TFLOP/s"},
+        {"hbm_ceiling", p.hbm_tflops, "TFLOP/s"},
+        {"tensor_peak", p.peak_tensor_tflops, "TFLOP/s"},
+        {"seconds", p.predicted_seconds, "s"},
+        {"mma_cycles_per_stage", p.t_mma_cycles, "cycles"},
+        {"smem_cycles_per_stage", p.t_smem_cycles, "cycles"},
+        {"fill_cycles_per_stage", p.t_l2_cycles, "cycles"},
+        {"stage_cycles", p.t_step_cycles, "cycles"},
+        {"ring_period_cycles", p.t_period_cycles, "cycles"},
+        {"epilogue_cycles_per_tile", p.t_epilogue_cycles, "cycles"},
+        {"tile_cycles", p.t_tile_cycles, "cycles"},
+        {"tiles", p.total_tiles, ""},
+        {"tile_slots", p.tile_slots, ""},
+        {"waves", p.waves_exact, ""},
+        {"wave_efficiency", p.wave_efficiency, ""},
+        {"smem_efficiency", p.smem_efficiency, ""},
+        {"fill_efficiency", p.l2_efficiency, ""},
+        {"latency_factor", p.occ_factor, ""},
+        {"epilogue_efficiency", p.epilogue_efficiency, ""},
+        {"envelope_efficiency", p.envelope_efficiency, ""},
+        {"dram_mbytes", p.dram_bytes / 1e6, "MB"},
+        {"flop_per_byte", p.arithmetic_intensity, ""},
+        {"ctas_per_sm", double(p.ctas_per_sm), ""},
+        {"accumulators", double(p.acc_buffers), ""},
+    };
+    if (o.json) {
+        std::printf("{\"gpu\": \"%s\", \"calibrated\": %s, \"M\": %lld, \"N\": %lld, \"K\": %lld, "
+                    "\"tile\": [%d, %d, %d, %d, %d, %d, %d, %d], \"fits\": %s, "
+                    "\"bottleneck\": \"%s\"",
+                    hw.name, hw.calibrated ? "true" : "false", (long long)g.M, (long long)g.N,
+                    (long long)g.K, g.tile.BM, g.tile.BN, g.tile.BK, g.tile.stages, g.tile.warps,
+                    g.tile.groupM, g.tile.cta_group, g.tile.split_k, fits ? "true" : "false",
+                    limiter);
+        for (const Item& it : items) std::printf(", \"%s\": %.9g", it.key, it.value);
+        std::printf("}\n");
+        return 0;
+    }
+    std::printf("%lld x %lld x %lld on %s (%s constants)\n", (long long)g.M, (long long)g.N,
+                (long long)g.K, hw.name, hw.calibrated ? "measured" : "built-in, unmeasured");
+    std::printf("tile BM=%d BN=%d BK=%d stages=%d warps=%d groupM=%d cta_group=%d split_k=%d\n",
+                g.tile.BM, g.tile.BN, g.tile.BK, g.tile.stages, g.tile.warps, g.tile.groupM,
+                g.tile.cta_group, g.tile.split_k);
+    if (!fits) {
+        std::printf("=> this tile does not fit on one SM (shared memory or Tensor Memory)\n");
+        return 0;
+    }
+    std::printf("=> %.1f TFLOP/s, limited by %s\n", p.predicted_tflops, limiter);
+    for (size_t i = 1; i < items.size(); ++i)
+        std::printf("   %-26s %14.4f %s\n", items[i].key, items[i].value, items[i].unit);
     return 0;
 }
 
 }  // namespace
 
 int main(int argc, char** argv) {
-    ridge_gemm_config cfg;
-    cfg.M = cfg.N = cfg.K = 4096;
-    cfg.tile = ridge_tile_config{128, 256, 64, 4, 4, 8, 0, 0};
-    std::string gpu = "b200", hw_path, batch_in, batch_out;
-    for (int i = 1; i < argc; ++i) {
-        const std::string a = argv[i];
-        auto next = [&](long long def) -> long long {
-            return (i + 1 < argc) ? std::atoll(argv[++i]) : def;
-        };
-        auto next_s = [&](const std::string& def) -> std::string {
-            return (i + 1 < argc) ? std::string(argv[++i]) : def;
-        };
-        if (a == "--gpu") gpu = next_s(gpu);
-        else if (a == "--hw") hw_path = next_s(hw_path);
-        else if (a == "--batch") batch_in = next_s(batch_in);
-        else if (a == "--out") batch_out = next_s(batch_out);
-        else if (a == "--m") cfg.M = next(cfg.M);
-        else if (a == "--n") cfg.N = next(cfg.N);
-        else if (a == "--k") cfg.K = next(cfg.K);
-        else if (a == "--bm") cfg.tile.BM = int(next(cfg.tile.BM));
-        else if (a == "--bn") cfg.tile.BN = int(next(cfg.tile.BN));
-        else if (a == "--bk") cfg.tile.BK = int(next(cfg.tile.BK));
-        else if (a == "--stages") cfg.tile.stages = int(next(cfg.tile.stages));
-        else if (a == "--warps") cfg.tile.warps = int(next(cfg.tile.warps));
-        else if (a == "--groupm") cfg.tile.groupM = int(next(cfg.tile.groupM));
-        else if (a == "--cta-group") cfg.tile.cta_group = int(next(cfg.tile.cta_group));
-        else if (a == "--split-k") cfg.tile.split_k = int(next(cfg.tile.split_k));
-        else if (a == "--warpm" || a == "--warpn" || a == "--regs") next(0);  // sm_80 only
-        else if (a == "-h" || a == "--help") {
-            usage();
-            return 0;
-        } else {
-            std::fprintf(stderr, "unknown arg: %s\n", a.c_str());
-            usage();
-            return 1;
-        }
-    }
-    ridge_hw hw;
-    if (!hw_path.empty()) {
-        char err[512];
-        if (ridge_hw_load_json(hw_path.c_str(), &hw, err, sizeof(err)) != RIDGE_OK) {
-            std::fprintf(stderr, "%s\n", err);
-            return 1;
-        }
-    } else if (gpu == "b200") {
-        ridge_hw_b200(&hw);
-    } else {
-        std::fprintf(stderr, "unknown gpu: %s\n", gpu.c_str());
-        return 1;
-    }
-    if (!batch_in.empty())
-        return run_batch(batch_in, batch_out.empty() ? "predictions.csv" : batch_out, hw, cfg);
-
-    ridge_prediction p;
-    if (ridge_predict(&cfg, &hw, &p) != RIDGE_OK) {
-        std::fprintf(stderr, "invalid shape\n");
-        return 1;
-    }
-    std::printf("GPU: %s\n", hw.name);
-    std::printf("  constants: %s\n", hw.calibrated ? "calibrated on a B200"
-                                                    : "datasheet placeholders, indicative only");
-    std::printf("GEMM %lldx%lldx%lld  tile %dx%dx%d  stages %d  warps %d  groupM %d  cta_group %d\n",
-                (long long)cfg.M, (long long)cfg.N, (long long)cfg.K, cfg.tile.BM, cfg.tile.BN,
-                cfg.tile.BK, cfg.tile.stages, cfg.tile.warps, cfg.tile.groupM, cfg.tile.cta_group);
-    if (p.bottleneck == RIDGE_BOTTLENECK_DOES_NOT_FIT) {
-        std::printf("  does not fit: shared memory or Tensor Memory exceed the SM\n");
+    Options o;
+    o.cfg.M = o.cfg.N = o.cfg.K = 4096;
+    o.cfg.tile = ridge_tile_config{128, 256, 64, 4, 4, 8, 0, 0};
+    if (!parse_args(argc, argv, o)) return 2;
+    if (o.help) {
+        std::fputs(kHelp, stdout);
         return 0;
     }
-    std::printf("  predicted:    %8.1f TFLOP/s   bottleneck: %s\n", p.predicted_tflops,
-                ridge_bottleneck_string(p.bottleneck));
-    std::printf("  peak tensor:  %8.1f   compute ceiling: %8.1f   HBM ceiling: %8.1f\n",
-                p.peak_tensor_tflops, p.compute_tflops, p.hbm_tflops);
-    std::printf("  per stage: mma %.0f  smem-read %.0f  TMA fill %.0f  -> %.0f cycles (period %.0f)\n",
-                p.t_mma_cycles, p.t_smem_cycles, p.t_l2_cycles, p.t_step_cycles,
-                p.t_period_cycles);
-    std::printf("  per tile: epilogue %.0f  tile %.0f cycles   %d accumulator(s)   CTAs/SM %d\n",
-                p.t_epilogue_cycles, p.t_tile_cycles, p.acc_buffers, p.ctas_per_sm);
-    std::printf("  grid: %.0f tiles in %.0f slots  waves %.2f  wave eff %.3f\n", p.total_tiles,
-                p.tile_slots, p.waves_exact, p.wave_efficiency);
-    std::printf("  effs: smem %.2f  fill %.2f  latency %.2f  epilogue %.2f  envelope %.3f\n",
-                p.smem_efficiency, p.l2_efficiency, p.occ_factor, p.epilogue_efficiency,
-                p.envelope_efficiency);
-    std::printf("  DRAM %.1f MB  arithmetic intensity %.1f FLOP/byte\n", p.dram_bytes / 1e6,
-                p.arithmetic_intensity);
-    return 0;
+    ridge_hw hw;
+    if (!load_hardware(o, &hw)) return 1;
+    return o.batch_in.empty() ? report_one(o, hw) : join_csv(o, hw);
 }

@@ -8,7 +8,7 @@ live in data/sweep/b200-ncu-configs.csv and the table below (RULES) was
 committed with them before the first run; `collect` only gathers counters and
 `score` only applies RULES. Neither may be edited to improve a result.
 
-    python -m ridge_b200.ncu_validate collect --out gpurun_out/ncu-labels.csv   # on a B200
+    python -m ridge_b200.ncu_validate collect --out ncu-labels.csv   # on a B200
     python -m ridge_b200.ncu_validate score data/measured/b200-ncu-labels.csv
 
 `collect` runs every configuration once without the profiler (the same command
@@ -179,7 +179,8 @@ def main(argv=None):
     o.add_argument("K", type=int)
     o.add_argument("config")
     c = sub.add_parser("collect")
-    c.add_argument("--out", default=str(ROOT / "gpurun_out" / "ncu-labels.csv"))
+    c.add_argument("--out", default="ncu-labels.csv",
+                   help="CSV of counters per configuration (default: ./ncu-labels.csv)")
     s = sub.add_parser("score")
     s.add_argument("path")
     a = ap.parse_args(argv)
