@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -165,6 +166,21 @@ int make_operand_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t co
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     return r == CUDA_SUCCESS ? RIDGE_OK : RIDGE_EINVAL;
+}
+
+// Producer threads issuing TMA loads: 1 (default), 2 or 4, read once from
+// RIDGE_TMA_ISSUERS (a knob for measurement). Measured on the GEMM itself, one
+// issuing thread keeps the ring as full as four: the loads are asynchronous,
+// and several issuing lanes of one warp spinning on different stage barriers
+// only diverge (256x256x128 pair tile, L2-flushed launches: 1385 against 1340
+// TFLOP/s at 4096^3, 1547 against 1391-1418 at 8192^3).
+int tma_issuers() {
+    static const int n = [] {
+        const char* v = std::getenv("RIDGE_TMA_ISSUERS");
+        const int x = v ? std::atoi(v) : 1;
+        return (x == 1 || x == 2 || x == 4) ? x : 1;
+    }();
+    return n;
 }
 
 // BM=256 tiles default to the 2-CTA pair (half the shared-memory operand
@@ -503,6 +519,7 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     p.stages = cfg->stages;
     p.tma_store = tma_store ? 1 : 0;
     p.epi_stride = plan.epi_stride;
+    p.tma_issuers = tma_issuers();
     p.num_peers = num_peers;
     p.err = dev->err_word;
     p.dp_tiles = plan.dp_tiles;

@@ -128,6 +128,7 @@ struct GemmParams {
     int stages;
     int tma_store;  // 1: epilogue stores through the C tensor map; 0: direct st.global
     int epi_stride; // staging bytes per epilogue warp: 4096, or 8192 for two pair buffers
+    int tma_issuers; // producer threads issuing TMA loads: 1, 2 or 4
     int num_peers;  // destinations in PeerMaps besides tmap_c (TMA-store epilogue only)
     int* err;
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
@@ -263,18 +264,19 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     const int unit = blockIdx.x / CG;
     const int num_units = gridDim.x / CG;
 
-    if (warp == 0 && lane < 4) {
+    if (warp == 0 && lane < p.tma_issuers) {
         // ------------------------------------------------------ TMA producer
-        // Four issuing threads. One thread completes only about one TMA box
-        // every ~800 cycles whatever the box size or ring depth (measured by
-        // the calibration benchmark), so stages alternate between two lane
-        // pairs, and within a pair lane 2p loads A (and arms the stage
-        // barrier) while lane 2p+1 loads B. In a 2-CTA pair both CTAs' loads
-        // complete on the leader's full barrier, armed with the bytes of both.
-        // A load may complete before its phase is armed; the phase cannot
-        // finish before the arming lane arrives.
-        const bool loads_a = (lane & 1) == 0;
-        const int my_pair = lane >> 1;
+        // tma_issuers (1, 2 or 4) issuing threads. With 4, stages alternate
+        // between two lane pairs; with 2 or 4, lane 2p of a pair loads A (and
+        // arms the stage barrier) while lane 2p+1 loads B; with 1, lane 0
+        // loads both. In a 2-CTA pair both CTAs' loads complete on the
+        // leader's full barrier, armed with the bytes of both. A load may
+        // complete before its phase is armed; the phase cannot finish before
+        // the arming lane arrives.
+        const int npairs = p.tma_issuers >= 4 ? 2 : 1;
+        const bool single = p.tma_issuers == 1;
+        const bool loads_a = single || (lane & 1) == 0;
+        const int my_pair = single ? 0 : lane >> 1;
         const uint32_t leader_full0 = CG == 2 ? map_to_cta(full_bar(0), 0) : full_bar(0);
         int stage = 0;
         uint32_t phase = 0;
@@ -287,7 +289,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             const int a_row = tm * BM + int(rank) * T::kRowsA;
             const int b_row = tn * BN + int(rank) * T::kRowsB;
             for (int kb = w.kb0; kb < w.kb1; ++kb) {
-                if (int(issued & 1) == my_pair) {
+                if (int(issued % npairs) == my_pair) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err,
                                    kErrTimeoutProducer)) {
                         ok = false;
@@ -298,21 +300,25 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                         CG == 1 ? full_bar(stage) : leader_full0 + 8u * uint32_t(stage);
                     if (loads_a && leader)
                         mbar_arrive_expect_tx(full_bar(stage), CG * T::kStageBytes);
-                    const uint32_t dst = loads_a ? sa : sa + T::kTileABytes;
-                    const void* map = loads_a ? static_cast<const void*>(&tmap_a)
-                                              : static_cast<const void*>(&tmap_b);
-                    const int row = loads_a ? a_row : b_row;
-                    if constexpr (T::kAtoms == 1) {
-                        if constexpr (CG == 1)
-                            tma_load_2d(dst, map, fb, kb * BK, row);
-                        else
-                            tma_load_2d_pair(dst, map, fb, kb * BK, row);
-                    } else {
-                        if constexpr (CG == 1)
-                            tma_load_3d(dst, map, fb, 0, row, kb * T::kAtoms);
-                        else
-                            tma_load_3d_pair(dst, map, fb, 0, row, kb * T::kAtoms);
-                    }
+                    auto load = [&](bool a_side) {
+                        const uint32_t dst = a_side ? sa : sa + T::kTileABytes;
+                        const void* map = a_side ? static_cast<const void*>(&tmap_a)
+                                                 : static_cast<const void*>(&tmap_b);
+                        const int row = a_side ? a_row : b_row;
+                        if constexpr (T::kAtoms == 1) {
+                            if constexpr (CG == 1)
+                                tma_load_2d(dst, map, fb, kb * BK, row);
+                            else
+                                tma_load_2d_pair(dst, map, fb, kb * BK, row);
+                        } else {
+                            if constexpr (CG == 1)
+                                tma_load_3d(dst, map, fb, 0, row, kb * T::kAtoms);
+                            else
+                                tma_load_3d_pair(dst, map, fb, 0, row, kb * T::kAtoms);
+                        }
+                    };
+                    load(loads_a);
+                    if (single) load(false);
                 }
                 ++issued;
                 if (++stage == stages) {
@@ -330,7 +336,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             // and this lane armed the slots with i & 1 == my_pair.
             const long long first = issued > stages ? issued - stages : 0;
             for (long long i = first; i < issued; ++i) {
-                if (int(i & 1) != my_pair) continue;
+                if (int(i % npairs) != my_pair) continue;
                 mbar_wait(full_bar(int(i % stages)), uint32_t((i / stages) & 1), nullptr, p.err,
                           kErrTimeoutDrain);
             }
