@@ -31,6 +31,10 @@ int noalloc_fill_counters(int byte);  // gemm_noalloc.cu
 // Per-device error word written by kernels whose bounded waits expire.
 __device__ int g_ridge_device_err = 0;
 
+#ifdef RIDGE_TRACE
+__device__ unsigned long long g_ridge_trace[512][64];
+#endif
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -397,7 +401,7 @@ int make_plan(const ridge_tile_config& cfg, int64_t M, int64_t N, int64_t K, Dev
     // area sits at a fixed offset so that every config sharing a workspace
     // finds it zeroed (the last arrival resets each counter; partials never
     // overlap it).
-    if (rem * e->cta_group * e->warps * 4 > kCounterBytes) {
+    if (rem * e->cta_group * e->warps * 8 > kCounterBytes) {  // two ints per warp
         plan->dp_tiles = int(tiles);
         plan->sk_tiles = 0;
         plan->sk_splits = 1;
@@ -695,6 +699,21 @@ int ridge_selftest_wait_timeout(int64_t limit_ns, int32_t* code, int64_t* waited
     // the wait must have given up (not completed) and raised the abort flag
     return ab == 1 ? RIDGE_OK : RIDGE_EDEVICE;
 }
+
+#ifdef RIDGE_TRACE
+// Timeline probe readout (trace builds only): copies and clears the per-CTA
+// stamps of the last launch.
+int ridge_trace_read(void* host, int64_t bytes) {
+    if (bytes < int64_t(sizeof(g_ridge_trace))) return RIDGE_EINVAL;
+    cudaError_t e = cudaMemcpyFromSymbol(host, g_ridge_trace, sizeof(g_ridge_trace));
+    if (e == cudaSuccess) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_ridge_trace);
+        if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(g_ridge_trace));
+    }
+    return int(e);
+}
+#endif
 
 int ridge_device_error(int clear, int32_t* code) {
     int st = RIDGE_OK;

@@ -133,12 +133,14 @@ struct GemmParams {
     int* err;
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
     // one per unit per round; the remaining sk_tiles tiles are each split into
-    // sk_splits contiguous K ranges, one range per unit, in a single last
-    // round. Every split publishes its FP32 partial into its own slot of
-    // `workspace` and then takes a ticket from counters[(sk * CG + rank) *
-    // warps + warp]; the warp holding the last ticket adds all slots in split
-    // order and stores C, then resets the counter to 0, so it starts at 0
-    // every launch. No split ever waits for another.
+    // sk_splits contiguous K ranges, one range per unit, which that unit
+    // computes before its whole tiles. Each epilogue warp of a split takes a ticket from
+    // counters[2 * ((sk * CG + rank) * warps + warp)] when its accumulator is
+    // ready; all but the last publish their FP32 partial into their split's
+    // slot of `workspace` and count it in the next int; the last waits for
+    // those (they are already running), folds them into its registers in
+    // split order and stores C, then resets both ints to 0, so they start at
+    // 0 every launch.
     int dp_tiles;
     int sk_tiles;
     int sk_splits;
@@ -154,6 +156,20 @@ struct WorkItem {
 
 __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_units, int num_kb,
                                          int i, WorkItem& w) {
+    // A unit with a split-K range does it first: its partial exchange and
+    // reduction then overlap the unit's whole tiles (the other TMEM
+    // accumulator), instead of trailing after the last MMA.
+    if (unit < p.sk_tiles * p.sk_splits) {
+        if (i == 0) {
+            w.sk = unit / p.sk_splits;
+            w.split = unit - w.sk * p.sk_splits;
+            w.tile = p.dp_tiles + w.sk;
+            w.kb0 = int((long long)num_kb * w.split / p.sk_splits);
+            w.kb1 = int((long long)num_kb * (w.split + 1) / p.sk_splits);
+            return true;
+        }
+        --i;
+    }
     const int dp_count = p.dp_tiles > unit ? (p.dp_tiles - unit + num_units - 1) / num_units : 0;
     if (i < dp_count) {
         w.tile = unit + i * num_units;
@@ -163,15 +179,13 @@ __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_
         w.sk = -1;
         return true;
     }
-    if (i == dp_count && unit < p.sk_tiles * p.sk_splits) {
-        w.sk = unit / p.sk_splits;
-        w.split = unit - w.sk * p.sk_splits;
-        w.tile = p.dp_tiles + w.sk;
-        w.kb0 = int((long long)num_kb * w.split / p.sk_splits);
-        w.kb1 = int((long long)num_kb * (w.split + 1) / p.sk_splits);
-        return true;
-    }
     return false;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
 }
 
 // Grouped-M tile order, the same mapping as the reference launch order
@@ -193,6 +207,22 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
 }
+
+#ifdef RIDGE_TRACE
+// Timeline probe (built only with -DRIDGE_TRACE, never in the library): per
+// CTA, [0] entry, [1 + i] MMA issue of item i done, [32 + i] epilogue of item i
+// done (warp 2), [63] exit, in %globaltimer nanoseconds.
+// (relocatable device code: defined once, in gemm_host.cu)
+extern __device__ unsigned long long g_ridge_trace[512][64];
+#define RIDGE_TRACE_AT(slot)                                                   \
+    do {                                                                       \
+        if (blockIdx.x < 512) g_ridge_trace[blockIdx.x][(slot)] = global_timer_ns(); \
+    } while (0)
+#else
+#define RIDGE_TRACE_AT(slot) \
+    do {                     \
+    } while (0)
+#endif
 
 template <int BM, int BN, int BK, int WARPS, int CG>
 __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
@@ -228,6 +258,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
     const bool leader = rank == 0;
 
     if (threadIdx.x == 0) {
+        RIDGE_TRACE_AT(0);
         for (int s = 0; s < stages; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
@@ -394,6 +425,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
             }
             if (!ok) break;
+            if (it < 31) RIDGE_TRACE_AT(1 + it);
             // Accumulator ready for the epilogue (of both CTAs of a pair).
             if constexpr (CG == 1)
                 umma_commit(tfull_bar(acc));
@@ -438,13 +470,13 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             if (!ok) break;
             tc_fence_after();
             // Split-K bookkeeping for this item: where the tile's FP32 partial
-            // slots live (one per split, in split order) and the counter that
-            // tickets this warp's arrivals.
+            // slots live (one per split, in split order) and this warp's two
+            // counters: [0] tickets the arrivals, [1] counts published partials.
             constexpr long long kTileFloats = T::kPartialFloats;
             float* ws_tile = nullptr;
             int* counter = nullptr;
             if (w.split >= 0) {
-                counter = p.counters + (w.sk * CG + int(rank)) * WARPS + epi;
+                counter = p.counters + 2 * ((w.sk * CG + int(rank)) * WARPS + epi);
                 const long long slot0 = (long long)w.sk * p.sk_splits;
                 ws_tile = p.workspace + (slot0 * CG + rank) * kTileFloats;
             }
@@ -502,38 +534,51 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 for (int e = 0; e < 16; ++e)
                     packed[e] = pack_half2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
             };
-            // Last arrival of a split tile: the sum of every split's partial,
-            // added in split order (the same order whichever split arrives last,
-            // so the result is deterministic), packed to FP16.
-            auto fold_ws = [&](int ci, uint32_t (&packed)[16]) {
-                float4 acc[8];
+            // Last arrival of a split tile: r holds this split's own partial
+            // (split w.split); fold in every other split's published partial so
+            // that r becomes p_0 + p_1 + ... + p_{s-1} added left to right in
+            // split order -- the same sum whichever split arrives last, so the
+            // result is deterministic. The prefix before w.split is summed
+            // apart, then added to r (x + y == y + x exactly), and the later
+            // partials are added to r in place.
+            auto fold_into = [&](int ci, uint32_t (&r)[32]) {
+                if (!warp_live_of(ci)) return;
+                auto src = [&](int sp) {
+                    return reinterpret_cast<const float4*>(
+                        ws_tile + (long long)sp * CG * kTileFloats + ws_offset(ci));
+                };
+                auto add_into_r = [&](const float4 (&q)[8]) {
 #pragma unroll
-                for (int v = 0; v < 8; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (warp_live_of(ci)) {
-                    for (int sp = 0; sp < p.sk_splits; ++sp) {
-                        const float4* src = reinterpret_cast<const float4*>(
-                            ws_tile + (long long)sp * CG * kTileFloats + ws_offset(ci));
+                    for (int v = 0; v < 8; ++v) {
+                        r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + q[v].x);
+                        r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + q[v].y);
+                        r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + q[v].z);
+                        r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + q[v].w);
+                    }
+                };
+                if (w.split > 0) {
+                    float4 pre[8];
+#pragma unroll
+                    for (int v = 0; v < 8; ++v) pre[v] = __ldcg(src(0) + v * 32);
+                    for (int sp = 1; sp < w.split; ++sp) {
                         float4 q[8];
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) q[v] = __ldcg(src + v * 32);
-                        if (sp == 0) {
+                        for (int v = 0; v < 8; ++v) q[v] = __ldcg(src(sp) + v * 32);
 #pragma unroll
-                            for (int v = 0; v < 8; ++v) acc[v] = q[v];
-                        } else {
-#pragma unroll
-                            for (int v = 0; v < 8; ++v) {
-                                acc[v].x += q[v].x;
-                                acc[v].y += q[v].y;
-                                acc[v].z += q[v].z;
-                                acc[v].w += q[v].w;
-                            }
+                        for (int v = 0; v < 8; ++v) {
+                            pre[v].x += q[v].x;
+                            pre[v].y += q[v].y;
+                            pre[v].z += q[v].z;
+                            pre[v].w += q[v].w;
                         }
                     }
+                    add_into_r(pre);
                 }
+                for (int sp = w.split + 1; sp < p.sk_splits; ++sp) {
+                    float4 q[8];
 #pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                    packed[2 * v] = pack_half2(acc[v].x, acc[v].y);
-                    packed[2 * v + 1] = pack_half2(acc[v].z, acc[v].w);
+                    for (int v = 0; v < 8; ++v) q[v] = __ldcg(src(sp) + v * 32);
+                    add_into_r(q);
                 }
             };
             auto store_chunk = [&](int ci, const uint32_t (&packed)[16]) {
@@ -673,36 +718,71 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
             load_group(0);
             wait_group();
             if (w.split >= 0) {
-                // Split-K item (warp-uniform branch). Publish this split's
-                // partial, then take a ticket; the split whose ticket comes
-                // last folds every slot and stores C. Nobody waits on another
-                // CTA, so split ranges need not be resident at the same time.
-#pragma unroll 1
-                for (int ci = 0; ci < kPerWarp; ci += kLd) {
-                    publish(ci, ra);
-                    if constexpr (kLd == 2) publish(ci + 1, rb);
-                    if (ci + kLd < kPerWarp) {
-                        __syncwarp();
-                        load_group(ci + kLd);
-                        wait_group();
-                    }
-                }
-                release_acc();
-                __threadfence();  // this warp's partial is visible before its ticket
-                __syncwarp();
+                // Split-K item (warp-uniform branch). The warp takes a ticket
+                // as soon as its accumulator is ready. Every split but the
+                // last to arrive publishes its FP32 partial and counts it; the
+                // last waits for those s - 1 partials and folds them into its
+                // own accumulator registers, then stores C. The last only ever
+                // waits for splits that have already taken a ticket, i.e. that
+                // are running and past their MMAs, so no split needs another
+                // to be scheduled; the wait is bounded all the same.
                 int ticket = 0;
                 if (lane == 0) ticket = atomicAdd(counter, 1);
                 ticket = __shfl_sync(0xffffffffu, ticket, 0);
-                if (ticket == p.sk_splits - 1) {
-                    __threadfence();  // the other splits' partials, published before their tickets
+                if (ticket != p.sk_splits - 1) {
 #pragma unroll 1
                     for (int ci = 0; ci < kPerWarp; ci += kLd) {
-                        uint32_t pa[16], pb[16];
-                        fold_ws(ci, pa);
-                        if constexpr (kLd == 2) fold_ws(ci + 1, pb);
-                        store_group(ci, pa, pb);
+                        publish(ci, ra);
+                        if constexpr (kLd == 2) publish(ci + 1, rb);
+                        if (ci + kLd < kPerWarp) {
+                            __syncwarp();
+                            load_group(ci + kLd);
+                            wait_group();
+                        }
                     }
-                    if (lane == 0) *counter = 0;  // every split arrived: ready for the next launch
+                    release_acc();
+                    __threadfence();  // the partial is visible before it is counted
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(counter + 1, 1);
+                } else {
+                    if (lane == 0) {
+                        const int want = p.sk_splits - 1;
+                        if (ld_acquire_gpu(counter + 1) < want) {
+                            const uint64_t t0 = global_timer_ns();
+                            while (ld_acquire_gpu(counter + 1) < want) {
+                                if (*abort_flag) break;
+                                if (global_timer_ns() - t0 > RIDGE_WAIT_LIMIT_NS) {
+                                    *abort_flag = 1;
+                                    atomicCAS(p.err, 0, int(kErrTimeoutSplitK));
+                                    break;
+                                }
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    __threadfence();  // the partials published before the count
+#pragma unroll 1
+                    for (int ci = 0; ci < kPerWarp; ci += kLd) {
+                        const bool more = ci + kLd < kPerWarp;
+                        uint32_t pa[16], pb[16];
+                        fold_into(ci, ra);
+                        pack(ra, pa);
+                        if constexpr (kLd == 2) {
+                            fold_into(ci + 1, rb);
+                            pack(rb, pb);
+                        }
+                        if (more) {
+                            __syncwarp();
+                            load_group(ci + kLd);
+                        }
+                        store_group(ci, pa, pb);
+                        if (more) wait_group();
+                    }
+                    release_acc();
+                    if (lane == 0) {  // every split arrived: ready for the next launch
+                        counter[0] = 0;
+                        counter[1] = 0;
+                    }
                 }
             } else {
 #pragma unroll 1
@@ -720,6 +800,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
                 release_acc();
             }
+            if (warp == 2 && lane == 0 && it < 31) RIDGE_TRACE_AT(32 + it);
             if (++acc == T::kAccBufs) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -741,6 +822,7 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
         tc_fence_after();
         tmem_dealloc<CG>(tmem_base, T::kTmemCols);
     }
+    if (threadIdx.x == 0) RIDGE_TRACE_AT(63);
 }
 
 }  // namespace ridge_b200

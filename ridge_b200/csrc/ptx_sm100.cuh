@@ -22,7 +22,7 @@ enum DeviceErr : int {
     kErrTimeoutMma = 2,        // MMA issuer waited too long for a full stage / free accumulator
     kErrTimeoutEpilogue = 3,   // epilogue waited too long for a finished accumulator
     kErrTimeoutDrain = 4,      // abort path: in-flight copies did not land in time
-    kErrTimeoutSplitK = 5,     // unused since split-K tiles fold on last arrival (kept: code values are stable)
+    kErrTimeoutSplitK = 5,     // a split-K last arrival waited too long for the other splits' partials
     kErrSelfTest = 6,          // ridge_selftest_wait_timeout: the wait expired as intended
     kErrSelfTestStale = 7,     // ridge_selftest_stale_counters: planted stale split-K counters
 };
