@@ -134,7 +134,7 @@ struct GemmParams {
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
     // one per unit per round; the remaining sk_tiles tiles are each split into
     // sk_splits contiguous K ranges, one range per unit, which that unit
-    // computes before its whole tiles. Each epilogue warp of a split takes a ticket from
+    // computes before (sk_first) or after its whole tiles. Each epilogue warp of a split takes a ticket from
     // counters[2 * ((sk * CG + rank) * warps + warp)] when its accumulator is
     // ready; all but the last publish their FP32 partial into their split's
     // slot of `workspace` and count it in the next int; the last waits for
@@ -144,6 +144,7 @@ struct GemmParams {
     int dp_tiles;
     int sk_tiles;
     int sk_splits;
+    int sk_first;  // 1: a unit's split range precedes its whole tiles; 0: it follows them
     float* workspace;
     int* counters;
 };
@@ -156,18 +157,20 @@ struct WorkItem {
 
 __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_units, int num_kb,
                                          int i, WorkItem& w) {
-    // A unit with a split-K range does it first: its partial exchange and
-    // reduction then overlap the unit's whole tiles (the other TMEM
-    // accumulator), instead of trailing after the last MMA.
-    if (unit < p.sk_tiles * p.sk_splits) {
-        if (i == 0) {
-            w.sk = unit / p.sk_splits;
-            w.split = unit - w.sk * p.sk_splits;
-            w.tile = p.dp_tiles + w.sk;
-            w.kb0 = int((long long)num_kb * w.split / p.sk_splits);
-            w.kb1 = int((long long)num_kb * (w.split + 1) / p.sk_splits);
-            return true;
-        }
+    const bool has_split = unit < p.sk_tiles * p.sk_splits;
+    auto split_item = [&]() {
+        w.sk = unit / p.sk_splits;
+        w.split = unit - w.sk * p.sk_splits;
+        w.tile = p.dp_tiles + w.sk;
+        w.kb0 = int((long long)num_kb * w.split / p.sk_splits);
+        w.kb1 = int((long long)num_kb * (w.split + 1) / p.sk_splits);
+        return true;
+    };
+    // With sk_first a unit's split-K range comes before its whole tiles, so
+    // its partial exchange overlaps the next tile's MMAs on the other TMEM
+    // accumulator instead of trailing the last one; otherwise it comes last.
+    if (has_split && p.sk_first) {
+        if (i == 0) return split_item();
         --i;
     }
     const int dp_count = p.dp_tiles > unit ? (p.dp_tiles - unit + num_units - 1) / num_units : 0;
@@ -179,6 +182,7 @@ __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_
         w.sk = -1;
         return true;
     }
+    if (has_split && !p.sk_first && i == dp_count) return split_item();
     return false;
 }
 

@@ -245,3 +245,30 @@ def test_split_k_launches_overlap_on_two_streams():
         assert rb.device_error() == 0
         assert_close(to_host_bits(outs[0]), ref1, "stream 1")
         assert_close(to_host_bits(outs[1]), ref2, "stream 2")
+
+
+# Split tails after many whole-tile rounds: the launcher puts split ranges
+# after the whole tiles there (with few rounds it puts them first).
+MANY_ROUND_CASES = [
+    ((3072, 11648, 1024), (128, 128, 32, 3, 4, 8)),        # 7 rounds of 296 units + 112 split
+    ((6400, 6400, 1024), (256, 256, 128, 3, 8, 8, 2)),     # 8 rounds of 74 pairs + 33 split
+]
+
+
+@pytest.mark.parametrize("shape,c", MANY_ROUND_CASES, ids=lambda x: "x".join(map(str, x)))
+def test_split_k_after_many_rounds(shape, c):
+    import ctypes
+    M, N, K = shape
+    cfg = _cfg(*c)
+    ws = ctypes.c_int64(0)
+    cc = cfg.to_c()
+    assert rb.lib.ridge_gemm_workspace_size(ctypes.byref(cc), M, N, K, ctypes.byref(ws)) == 0
+    assert ws.value > 0, "expected this case to split"
+    a, b = oracle.unit_inputs(M, N, K, seed=41)
+    rows = np.unique(np.concatenate([np.arange(8), np.arange(M - 8, M),
+                                     np.random.default_rng(3).choice(M, 48, replace=False)]))
+    ref = oracle.gemm_f64(a, b, rows=rows)
+    ad, bd = to_dev(a), to_dev(b)
+    for _ in range(2):
+        out = run_gemm(cfg, ad, bd, M, N, K)
+        assert_close(to_host_bits(out)[rows], ref, "split after rounds " + cfg.tag())
