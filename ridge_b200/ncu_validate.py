@@ -10,6 +10,13 @@ committed with them before the first run; `collect` only gathers counters and
 
     python -m ridge_b200.ncu_validate collect --out ncu-labels.csv   # on a B200
     python -m ridge_b200.ncu_validate score data/measured/b200-ncu-labels.csv
+    python -m ridge_b200.ncu_validate table --out ncu-table.csv       # on a B200
+    python -m ridge_b200.ncu_validate render data/measured/b200-ncu-table.csv
+
+`table` gathers a per-configuration counter table (tensor pipe, DRAM bytes
+and GB/s, L2 -> SM bytes, shared-memory wavefronts of the tensor-core data
+path) for the configurations in data/sweep/b200-ncu-table.csv, the same way
+(plain run first, then one captured launch); `render` prints it as Markdown.
 
 `collect` runs every configuration once without the profiler (the same command
 line), and only if that exits 0 runs it under
@@ -31,6 +38,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent.parent
 CONFIGS = ROOT / "data" / "sweep" / "b200-ncu-configs.csv"
+TABLE_CONFIGS = ROOT / "data" / "sweep" / "b200-ncu-table.csv"
 
 METRICS = [
     "gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed",
@@ -39,6 +47,20 @@ METRICS = [
     "l1tex__m_xbar2l1tex_read_bytes.sum",
     "l1tex__m_l1tex2xbar_write_bytes.sum",
     "sm__cycles_active.sum",
+]
+
+# Counters of the per-configuration table.
+TABLE_METRICS = [
+    "gpu__time_duration.sum",
+    "sm__cycles_elapsed.avg.per_second",
+    "sm__cycles_active.avg.pct_of_peak_sustained_elapsed",
+    "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active",
+    "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed",
+    "dram__bytes_read.sum",
+    "dram__bytes_write.sum",
+    "gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed",
+    "l1tex__m_xbar2l1tex_read_bytes.sum",
+    "l1tex__data_pipe_tc_wavefronts_mem_shared.sum",
 ]
 
 # The registered thresholds.
@@ -145,6 +167,82 @@ def collect(out_path, configs=CONFIGS, log=print):
     return out_path
 
 
+def _ncu_metrics(cmd, metrics, ncu):
+    """Plain run of `cmd` first; only if it exits 0, one captured launch of the
+    GEMM (the second; the first is a warm-up) with `metrics`. Returns the
+    counters (name -> float, in ncu's base units), or an error string."""
+    plain = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+    if plain.returncode != 0:
+        return "plain run failed (%d): %s" % (plain.returncode, plain.stderr[-500:])
+    prof = subprocess.run([ncu, "--csv", "--print-units", "base", "--clock-control", "none",
+                           "--metrics", ",".join(metrics), "-k", "regex:ridge_gemm_sm100", "-s",
+                           "1", "-c", "1", *cmd], capture_output=True, text=True, timeout=600)
+    lines = [l for l in prof.stdout.splitlines() if l.startswith('"')]
+    vals = {}
+    for row in csv.DictReader(io.StringIO("\n".join(lines))):
+        name, val = row.get("Metric Name"), row.get("Metric Value")
+        if name in metrics and val not in (None, ""):
+            vals[name] = float(val.replace(",", ""))
+    if len(vals) != len(metrics):
+        return "%d of %d counters (rc %d): %s" % (len(vals), len(metrics), prof.returncode,
+                                                 (prof.stdout + prof.stderr)[-500:])
+    return vals
+
+
+def table(out_path, configs=TABLE_CONFIGS, log=print):
+    ncu = shutil.which("ncu") or "/usr/local/cuda/bin/ncu"
+    rows = load_configs(configs)
+    out_path = Path(out_path)
+    out_path.parent.mkdir(parents=True, exist_ok=True)
+    with open(out_path, "w", newline="") as f:
+        w = csv.writer(f)
+        w.writerow(["tag", "M", "N", "K", "BM", "BN", "BK", "stages", "warps", "groupM",
+                    "cta_group", *TABLE_METRICS])
+        for i, r in enumerate(rows):
+            vals = _ncu_metrics(_cmd(r), TABLE_METRICS, ncu)
+            if isinstance(vals, str):
+                log("[%2d] %s: %s" % (i + 1, r["tag"], vals))
+                continue
+            w.writerow([r["tag"], r["M"], r["N"], r["K"], r["BM"], r["BN"], r["BK"], r["stages"],
+                        r["warps"], r["groupM"], r["cta_group"], *[vals[m] for m in TABLE_METRICS]])
+            f.flush()
+            log("[%2d] %s %sx%sx%s done" % (i + 1, r["tag"], r["BM"], r["BN"], r["BK"]))
+    return out_path
+
+
+def render(path, hbm_peak_gbs=None, log=print):
+    """The counter table as Markdown: per configuration the captured launch's
+    time, TFLOP/s, tensor-pipe share of active and elapsed cycles, DRAM bytes
+    and GB/s (and % of the measured copy peak when given), algorithmic bytes,
+    L2 -> SM bytes per SM cycle, and shared-memory wavefronts per SM cycle of
+    the tensor-core data path (128 B each)."""
+    with open(path, newline="") as f:
+        rows = list(csv.DictReader(l for l in f if not l.startswith("#")))
+    log("| cfg | shape | tile | us | TFLOP/s | tensor %% active | tensor %% elapsed | SM active %% "
+        "| DRAM MB (alg.) | DRAM GB/s%s | L2->SM B/clk/SM | smem wavefronts/clk/SM |"
+        % (" (%% of peak)" if hbm_peak_gbs else ""))
+    log("|---|---|---|---|---|---|---|---|---|---|---|---|")
+    for r in rows:
+        g = {k: float(r[k]) for k in TABLE_METRICS}
+        M, N, K = int(r["M"]), int(r["N"]), int(r["K"])
+        sec = g["gpu__time_duration.sum"] * 1e-9
+        cycles = sec * g["sm__cycles_elapsed.avg.per_second"] * 148
+        dram = g["dram__bytes_read.sum"] + g["dram__bytes_write.sum"]
+        alg = 2.0 * (M * K + N * K + M * N)
+        gbs = dram / sec / 1e9
+        log("| %s | %dx%dx%d | %sx%sx%s s%s w%s c%s | %.1f | %.0f | %.1f | %.1f | %.1f | %.1f (%.1f) "
+            "| %.0f%s | %.1f | %.2f |" % (
+                r["tag"], M, N, K, r["BM"], r["BN"], r["BK"], r["stages"], r["warps"],
+                r["cta_group"], sec * 1e6, 2.0 * M * N * K / sec / 1e12,
+                g["sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active"],
+                g["sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed"],
+                g["sm__cycles_active.avg.pct_of_peak_sustained_elapsed"], dram / 1e6, alg / 1e6,
+                gbs, (" (%.0f%%)" % (100.0 * gbs / hbm_peak_gbs)) if hbm_peak_gbs else "",
+                g["l1tex__m_xbar2l1tex_read_bytes.sum"] / cycles,
+                g["l1tex__data_pipe_tc_wavefronts_mem_shared.sum"] / cycles))
+    return len(rows)
+
+
 def score(path, log=print):
     with open(path, newline="") as f:
         rows = list(csv.DictReader(l for l in f if not l.startswith("#")))
@@ -183,7 +281,18 @@ def main(argv=None):
                    help="CSV of counters per configuration (default: ./ncu-labels.csv)")
     s = sub.add_parser("score")
     s.add_argument("path")
+    t = sub.add_parser("table")
+    t.add_argument("--out", default="ncu-table.csv")
+    r = sub.add_parser("render")
+    r.add_argument("path")
+    r.add_argument("--hbm-peak-gbs", type=float, default=None)
     a = ap.parse_args(argv)
+    if a.cmd == "table":
+        print("wrote", table(a.out))
+        return 0
+    if a.cmd == "render":
+        render(a.path, a.hbm_peak_gbs)
+        return 0
     if a.cmd == "one":
         run_one(a.M, a.N, a.K, tuple(int(x) for x in a.config.split(",")))
         return 0
