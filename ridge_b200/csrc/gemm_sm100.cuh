@@ -158,10 +158,14 @@ struct WorkItem {
 __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_units, int num_kb,
                                          int i, WorkItem& w) {
     const bool has_split = unit < p.sk_tiles * p.sk_splits;
+    // The split tiles are the first sk_tiles tiles of the grouped order when
+    // they run first (so they share L2 panels with the first whole tiles, run
+    // at the same time) and the last ones otherwise.
+    const int whole0 = p.sk_first ? p.sk_tiles : 0;
     auto split_item = [&]() {
         w.sk = unit / p.sk_splits;
         w.split = unit - w.sk * p.sk_splits;
-        w.tile = p.dp_tiles + w.sk;
+        w.tile = p.sk_first ? w.sk : p.dp_tiles + w.sk;
         w.kb0 = int((long long)num_kb * w.split / p.sk_splits);
         w.kb1 = int((long long)num_kb * (w.split + 1) / p.sk_splits);
         return true;
@@ -175,7 +179,7 @@ __device__ __forceinline__ bool get_item(const GemmParams& p, int unit, int num_
     }
     const int dp_count = p.dp_tiles > unit ? (p.dp_tiles - unit + num_units - 1) / num_units : 0;
     if (i < dp_count) {
-        w.tile = unit + i * num_units;
+        w.tile = whole0 + unit + i * num_units;
         w.kb0 = 0;
         w.kb1 = num_kb;
         w.split = -1;
