@@ -386,6 +386,11 @@ typedef struct ridge_tune_result {
  * `entries` (optional, capacity `entries_cap` per shape, row-major
  * [shape][entry]) receives every candidate in model-rank order.
  * timed_iters/warmup_iters control the per-candidate CUDA-event timing.
+ * A device that cannot be set up takes no part; a device that hits a CUDA
+ * error mid-sweep hands its candidate back to the queue for the other
+ * devices and retires. Returns RIDGE_OK when every selected candidate was
+ * measured (a candidate whose own launch timed out on the device is measured,
+ * with status RIDGE_EDEVICE), RIDGE_EDEVICE when some were left undone.
  */
 int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
                    const int32_t* devices, int32_t num_devices, const ridge_hw* hw,
@@ -402,6 +407,20 @@ int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
 int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                     int32_t warmup, int32_t iters, void* stream, double* ms_per_launch);
+
+/*
+ * Self-test of the autotuner's work queue on the host (no GPU, no counterpart
+ * in the reference): num_jobs fake jobs over num_devices fake devices, each
+ * job a short sleep (12 ms on slow_device, 2 ms elsewhere). lost_device fails
+ * after completing lost_after jobs, handing its current job back (lost_after
+ * < 0: it fails its set-up and takes no job). job_device[j] receives the
+ * device that completed job j (-1 if none), jobs_per_device[d] the jobs device
+ * d completed. Returns what ridge_autotune would: RIDGE_OK when every job was
+ * done, RIDGE_EDEVICE otherwise. Pass -1 for no lost / no slow device.
+ */
+int ridge_farm_selftest(int32_t num_jobs, int32_t num_devices, int32_t lost_device,
+                        int32_t lost_after, int32_t slow_device, int32_t* job_device,
+                        int32_t* jobs_per_device);
 
 /* ---------------------------------------------------------------- N-slab sharding */
 

@@ -137,6 +137,8 @@ SIGNATURES = {
     "ridge_autotune": (C.c_int, [C.POINTER(_i64), _i32, _i32, C.POINTER(_i32), _i32,
                                  C.POINTER(HwC), _i32, _i32, C.POINTER(TuneResultC),
                                  C.POINTER(TuneEntryC), _i32]),
+    "ridge_farm_selftest": (C.c_int, [_i32, _i32, _i32, _i32, _i32, C.POINTER(_i32),
+                                      C.POINTER(_i32)]),
     "ridge_time_gemm": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _i32, _vp, C.POINTER(C.c_double)]),
     "ridge_cal_umma": (C.c_int, [_i32, _i32, _i32, C.POINTER(C.c_double),

@@ -6,8 +6,10 @@
 // benchmarks on the GPU, from C++, and farms the (shape, candidate) jobs over
 // any number of devices: one host worker thread per device pulls jobs from a
 // shared queue, times each candidate with CUDA events on its own stream and
-// buffers, and writes the result into its slot. No collective is involved;
-// results are gathered on the host. k <= 0 benchmarks every candidate, which is
+// buffers, and writes the result into its slot. A device that cannot be set
+// up takes no part; one that fails mid-sweep hands its job back to the queue
+// for the others. No collective is involved; results are gathered on the
+// host. k <= 0 benchmarks every candidate, which is
 // the exhaustive sweep that regret is measured against.
 //
 // Timer: the reference's measure.cu:121-150 method -- warm-up launches, a short
@@ -18,8 +20,12 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
+#include <condition_variable>
 #include <cstring>
+#include <deque>
+#include <mutex>
 #include <numeric>
 #include <thread>
 #include <vector>
@@ -87,9 +93,106 @@ int time_on_stream(const ridge_tile_config* cfg, const void* A, const void* B, v
     return RIDGE_OK;
 }
 
+// ------------------------------------------------------------------ the farm
+//
+// Jobs 0..n-1 are handed out from one queue to one worker thread per device.
+// A worker first sets its device up (`setup`); if that fails the device takes
+// no part and the others carry on. `run(slot, job)` measures one job and says
+// what happened to the device:
+//   kDone        the job has its result (which may itself be a failure the
+//                device survived, e.g. a bounded device wait that expired);
+//   kDeviceLost  the device cannot go on (a sticky CUDA error): the job goes
+//                back to the queue for another device and this worker retires.
+// Workers leave only when the queue is empty and no job is in flight, so a
+// job returned by a device that is lost late is still picked up. A job that
+// every device lost stays undone.
+enum class Outcome { kDone, kDeviceLost };
+
+struct FarmState {
+    std::mutex mu;
+    std::condition_variable cv;
+    std::deque<int> pending;
+    int in_flight = 0;
+    int live = 0;  // workers still able to take jobs
+};
+
+// Returns RIDGE_OK when every job was done, RIDGE_EDEVICE otherwise. job_slot[j]
+// receives the worker slot (index into the device list) that completed job j,
+// or -1.
+template <class Setup, class Run, class Teardown>
+int run_farm(int num_jobs, int num_slots, Setup setup, Run run, Teardown teardown,
+             std::vector<int>& job_slot) {
+    FarmState f;
+    for (int j = 0; j < num_jobs; ++j) f.pending.push_back(j);
+    f.live = num_slots;
+    job_slot.assign(size_t(num_jobs), -1);
+    auto worker = [&](int slot) {
+        const bool ok = setup(slot);
+        for (;;) {
+            int job = -1;
+            if (ok) {
+                std::unique_lock<std::mutex> lock(f.mu);
+                f.cv.wait(lock, [&] { return !f.pending.empty() || f.in_flight == 0; });
+                if (f.pending.empty()) break;  // nothing queued and nothing can come back
+                job = f.pending.front();
+                f.pending.pop_front();
+                ++f.in_flight;
+            } else {
+                break;
+            }
+            const Outcome o = run(slot, job);
+            std::lock_guard<std::mutex> lock(f.mu);
+            --f.in_flight;
+            if (o == Outcome::kDone) {
+                job_slot[size_t(job)] = slot;
+            } else {
+                f.pending.push_front(job);  // another device will measure it
+                --f.live;
+                f.cv.notify_all();
+                teardown(slot);
+                return;
+            }
+            f.cv.notify_all();
+        }
+        {
+            std::lock_guard<std::mutex> lock(f.mu);
+            --f.live;
+            f.cv.notify_all();
+        }
+        teardown(slot);
+    };
+    std::vector<std::thread> pool;
+    for (int i = 0; i < num_slots; ++i) pool.emplace_back(worker, i);
+    for (auto& t : pool) t.join();
+    for (int j = 0; j < num_jobs; ++j)
+        if (job_slot[size_t(j)] < 0) return RIDGE_EDEVICE;
+    return RIDGE_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int ridge_farm_selftest(int32_t num_jobs, int32_t num_devices, int32_t lost_device,
+                        int32_t lost_after, int32_t slow_device, int32_t* job_device,
+                        int32_t* jobs_per_device) {
+    if (num_jobs < 0 || num_devices <= 0 || !job_device || !jobs_per_device) return RIDGE_EINVAL;
+    std::vector<std::atomic<int>> done(static_cast<size_t>(num_devices));
+    for (auto& d : done) d.store(0);
+    auto setup = [&](int slot) { return !(slot == lost_device && lost_after < 0); };
+    auto run = [&](int slot, int) {
+        if (slot == lost_device && done[size_t(slot)].load() >= lost_after)
+            return Outcome::kDeviceLost;
+        std::this_thread::sleep_for(std::chrono::milliseconds(slot == slow_device ? 12 : 2));
+        done[size_t(slot)].fetch_add(1);
+        return Outcome::kDone;
+    };
+    std::vector<int> job_slot;
+    const int st = run_farm(num_jobs, num_devices, setup, run, [](int) {}, job_slot);
+    for (int j = 0; j < num_jobs; ++j) job_device[j] = job_slot[size_t(j)];
+    for (int d = 0; d < num_devices; ++d) jobs_per_device[d] = done[size_t(d)].load();
+    return st;
+}
 
 int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, void* Cp,
                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
@@ -166,73 +269,55 @@ int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const i
     std::stable_sort(jobs.begin(), jobs.end(),
                      [](const Job& x, const Job& y) { return x.slot < y.slot; });
 
-    std::atomic<size_t> next{0};
-    std::atomic<int> fatal{RIDGE_OK};
-    auto worker = [&](int dev) {
-        cudaError_t ce = cudaSetDevice(dev);
-        if (ce != cudaSuccess) {
-            fatal.store(int(ce));
-            return;
-        }
-        DeviceBuffers d;
-        auto fail = [&](int code) {
-            int expect = RIDGE_OK;
-            fatal.compare_exchange_strong(expect, code);
-        };
-        if ((ce = cudaMalloc(&d.a, size_t(maxA) * 2)) != cudaSuccess ||
-            (ce = cudaMalloc(&d.b, size_t(maxB) * 2)) != cudaSuccess ||
-            (ce = cudaMalloc(&d.c, size_t(maxC) * 2)) != cudaSuccess ||
-            (ce = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking)) != cudaSuccess ||
-            (ce = cudaEventCreate(&d.e0)) != cudaSuccess ||
-            (ce = cudaEventCreate(&d.e1)) != cudaSuccess) {
-            fail(int(ce));
-        } else {
-            uint32_t state = 0;
-            int st = ridge_fill_lcg(d.a, maxA, &state, 1, d.stream);
-            if (st == RIDGE_OK) st = ridge_fill_lcg(d.b, maxB, &state, 1, d.stream);
-            if (st != RIDGE_OK) fail(st);
-            cudaStreamSynchronize(d.stream);
-            while (fatal.load() == RIDGE_OK) {
-                const size_t j = next.fetch_add(1);
-                if (j >= jobs.size()) break;
-                const Job& job = jobs[j];
-                ridge_tune_entry& e = cands[job.shape][job.slot];
-                const int64_t M = shapes[3 * job.shape], N = shapes[3 * job.shape + 1],
-                              K = shapes[3 * job.shape + 2];
-                double ms = 0;
-                const int ts = time_on_stream(&e.tile, d.a, d.b, d.c, M, N, K, K, K, N,
-                                              warmup_iters, timed_iters, d.stream, d.e0, d.e1,
-                                              &ms);
-                e.device = dev;
-                e.status = ts;
-                e.measured_tflops = ts == RIDGE_OK ? 2.0 * M * N * K / (ms * 1e-3) / 1e12 : 0.0;
-                int32_t code = 0;
-                // A CUDA error is sticky for this device's context: stop this
-                // worker, the others keep going. A device-side timeout (bounded
-                // wait) leaves the context usable: record it, clear it, go on.
-                if (ts > 0) break;
-                const int de = ridge_device_error(1, &code);
-                if (de != RIDGE_OK) {
-                    e.status = de;
-                    e.measured_tflops = 0.0;
-                    break;
-                }
-                if (code != 0) {
-                    e.status = RIDGE_EDEVICE;
-                    e.measured_tflops = 0.0;
-                }
-            }
-        }
+    std::vector<DeviceBuffers> bufs(static_cast<size_t>(num_devices));
+    auto setup = [&](int slot) {
+        DeviceBuffers& d = bufs[size_t(slot)];
+        cudaError_t ce = cudaSetDevice(devices[slot]);
+        if (ce == cudaSuccess) ce = cudaMalloc(&d.a, size_t(maxA) * 2);
+        if (ce == cudaSuccess) ce = cudaMalloc(&d.b, size_t(maxB) * 2);
+        if (ce == cudaSuccess) ce = cudaMalloc(&d.c, size_t(maxC) * 2);
+        if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
+        if (ce == cudaSuccess) ce = cudaEventCreate(&d.e0);
+        if (ce == cudaSuccess) ce = cudaEventCreate(&d.e1);
+        if (ce != cudaSuccess) return false;
+        uint32_t state = 0;
+        int st = ridge_fill_lcg(d.a, maxA, &state, 1, d.stream);
+        if (st == RIDGE_OK) st = ridge_fill_lcg(d.b, maxB, &state, 1, d.stream);
+        return st == RIDGE_OK && cudaStreamSynchronize(d.stream) == cudaSuccess;
+    };
+    auto run = [&](int slot, int j) {
+        DeviceBuffers& d = bufs[size_t(slot)];
+        const Job& job = jobs[size_t(j)];
+        ridge_tune_entry& e = cands[job.shape][job.slot];
+        const int64_t M = shapes[3 * job.shape], N = shapes[3 * job.shape + 1],
+                      K = shapes[3 * job.shape + 2];
+        double ms = 0;
+        const int ts = time_on_stream(&e.tile, d.a, d.b, d.c, M, N, K, K, K, N, warmup_iters,
+                                      timed_iters, d.stream, d.e0, d.e1, &ms);
+        // A CUDA error is sticky for this device's context: the job goes to
+        // another device. A device-side timeout (bounded wait) leaves the
+        // context usable: record it, clear it, go on.
+        if (ts > 0) return Outcome::kDeviceLost;
+        int32_t code = 0;
+        const int de = ridge_device_error(1, &code);
+        if (de != RIDGE_OK) return Outcome::kDeviceLost;
+        e.device = devices[slot];
+        e.status = ts != RIDGE_OK ? ts : (code != 0 ? RIDGE_EDEVICE : RIDGE_OK);
+        e.measured_tflops = e.status == RIDGE_OK ? 2.0 * M * N * K / (ms * 1e-3) / 1e12 : 0.0;
+        return Outcome::kDone;
+    };
+    auto teardown = [&](int slot) {
+        DeviceBuffers& d = bufs[size_t(slot)];
         if (d.e0) cudaEventDestroy(d.e0);
         if (d.e1) cudaEventDestroy(d.e1);
         if (d.stream) cudaStreamDestroy(d.stream);
         cudaFree(d.a);
         cudaFree(d.b);
         cudaFree(d.c);
+        d = DeviceBuffers();
     };
-    std::vector<std::thread> pool;
-    for (int i = 0; i < num_devices; ++i) pool.emplace_back(worker, devices[i]);
-    for (auto& t : pool) t.join();
+    std::vector<int> job_slot;
+    const int farm_status = run_farm(int(jobs.size()), num_devices, setup, run, teardown, job_slot);
 
     for (int s = 0; s < num_shapes; ++s) {
         ridge_tune_result& r = results[s];
@@ -260,7 +345,7 @@ int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const i
             }
         }
     }
-    return fatal.load();
+    return farm_status;
 }
 
 }  // extern "C"
