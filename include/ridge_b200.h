@@ -385,7 +385,9 @@ typedef struct ridge_tune_result {
  * keep the fastest. k <= 0 benchmarks every candidate (the exhaustive sweep).
  * `entries` (optional, capacity `entries_cap` per shape, row-major
  * [shape][entry]) receives every candidate in model-rank order.
- * timed_iters/warmup_iters control the per-candidate CUDA-event timing.
+ * Each candidate is timed by ridge_time_gemm_cold (warmup_iters launches, then
+ * at least timed_iters L2-flushed launches; a 256 MiB flush buffer per
+ * device), the discipline of the headline benchmark.
  * A device that cannot be set up takes no part; a device that hits a CUDA
  * error mid-sweep hands its candidate back to the queue for the other
  * devices and retires. Returns RIDGE_OK when every selected candidate was
@@ -407,6 +409,22 @@ int ridge_autotune(const int64_t* shapes_mnk, int32_t num_shapes, int32_t k,
 int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                     int32_t warmup, int32_t iters, void* stream, double* ms_per_launch);
+
+/*
+ * Cold timing, the headline benchmark's discipline (no counterpart in the
+ * reference, whose measure.cu times warm back-to-back launches): `warmup`
+ * launches, then launches each preceded by overwriting `flush_bytes` of the
+ * caller's `flush` buffer (make it larger than L2, e.g. 256 MiB, so A and B
+ * come from DRAM), with CUDA events around the launch alone: at least `iters`
+ * of them, more (up to 200) until about 2 ms of kernel time is sampled.
+ * *ms_per_launch = the mean of the middle 60% of those launch times (single
+ * event times are quantised to about 1 us). Allocates nothing. Synchronises
+ * the stream.
+ */
+int ridge_time_gemm_cold(const ridge_tile_config* cfg, const void* A, const void* B, void* C,
+                         int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                         void* flush, int64_t flush_bytes, int32_t warmup, int32_t iters,
+                         void* stream, double* ms_per_launch);
 
 /*
  * Self-test of the autotuner's work queue on the host (no GPU, no counterpart

@@ -141,6 +141,9 @@ SIGNATURES = {
                                       C.POINTER(_i32)]),
     "ridge_time_gemm": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i32, _i32, _vp, C.POINTER(C.c_double)]),
+    "ridge_time_gemm_cold": (C.c_int, [C.POINTER(TileConfigC), _vp, _vp, _vp, _i64, _i64, _i64,
+                                       _i64, _i64, _i64, _vp, _i64, _i32, _i32, _vp,
+                                       C.POINTER(C.c_double)]),
     "ridge_cal_umma": (C.c_int, [_i32, _i32, _i32, C.POINTER(C.c_double),
                                  C.POINTER(C.c_double)]),
     "ridge_cal_tma": (C.c_int, [_i64, _i32, _i32, _i32, _i32, _i32, _i32, C.POINTER(C.c_double),

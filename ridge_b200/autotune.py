@@ -55,7 +55,9 @@ def load_sweep(path=REGISTERED):
 
 def autotune(shapes, k=10, devices=(0,), hw: HwC | None = None, warmup=3, iters=10):
     """Runs the farm. Returns (results, entries): per shape the best measured
-    config, and every ranked candidate (benchmarked or not) in model order."""
+    config, and every ranked candidate (benchmarked or not) in model order.
+    Each benchmarked candidate is timed over L2-flushed launches (at least
+    `iters`; ridge_time_gemm_cold)."""
     hw = hw if hw is not None else default_hw()
     n = len(shapes)
     mnk = (C.c_int64 * (3 * n))(*[v for s in shapes for v in s[:3]])
@@ -167,20 +169,24 @@ CANARY = (4096, 4096, 4096)
 
 
 def canary_tflops(device=0):
-    """A fixed 4096^3 launch (the bench tile) timed on `device`: the drift check
-    of the reference's measure.cu, between shapes of a long sweep."""
+    """A fixed 4096^3 launch (the bench tile) timed cold on `device` -- the
+    drift check of the reference's measure.cu, between shapes of a long sweep."""
     import torch
 
-    from .gemm import DEFAULT_CONFIG, synthetic_inputs
+    from .gemm import synthetic_inputs
     M, N, K = CANARY
+    cfg = TileConfig(256, 256, 128, 3, 8, 8, 2)
     with torch.cuda.device(device):
-        a, b = synthetic_inputs(M, N, K, device=torch.device("cuda", device))
-        c = torch.empty((M, N), dtype=torch.float16, device=a.device)
+        dev = torch.device("cuda", device)
+        a, b = synthetic_inputs(M, N, K, device=dev)
+        c = torch.empty((M, N), dtype=torch.float16, device=dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         ms = C.c_double()
-        cc = DEFAULT_CONFIG.to_c()
-        check(lib.ridge_time_gemm(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N,
-                                  K, K, K, N, 5, 20, torch.cuda.current_stream().cuda_stream,
-                                  C.byref(ms)), "canary")
+        cc = cfg.to_c()
+        check(lib.ridge_time_gemm_cold(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M,
+                                       N, K, K, K, N, flush.data_ptr(), flush.numel(), 3, 20,
+                                       torch.cuda.current_stream().cuda_stream, C.byref(ms)),
+              "canary")
     return 2.0 * M * N * K / (ms.value * 1e-3) / 1e12
 
 

@@ -12,9 +12,12 @@
 // host. k <= 0 benchmarks every candidate, which is
 // the exhaustive sweep that regret is measured against.
 //
-// Timer: the reference's measure.cu:121-150 method -- warm-up launches, a short
-// probe to size the run, then an adaptive number of back-to-back launches
-// between two events -- repeated three times, keeping the fastest.
+// Timers: ridge_time_gemm follows the reference's measure.cu:121-150 method --
+// warm-up launches, a short probe to size the run, then an adaptive number of
+// back-to-back launches between two events -- repeated three times, keeping
+// the fastest. The farm times every candidate the way the headline benchmark
+// times the GEMM instead (ridge_time_gemm_cold): each launch after an L2 flush,
+// events around the launch alone, the median launch.
 
 #include <cuda_runtime.h>
 
@@ -47,8 +50,9 @@ struct DeviceBuffers {
     void* a = nullptr;
     void* b = nullptr;
     void* c = nullptr;
+    void* flush = nullptr;  // overwritten before every timed launch
     cudaStream_t stream = nullptr;
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    std::vector<cudaEvent_t> ev;
 };
 
 int time_on_stream(const ridge_tile_config* cfg, const void* A, const void* B, void* Cp,
@@ -92,6 +96,66 @@ int time_on_stream(const ridge_tile_config* cfg, const void* A, const void* B, v
     *ms_out = best;
     return RIDGE_OK;
 }
+
+// Cold timing, the discipline of the headline benchmark: before every launch
+// `flush_bytes` of `flush` are overwritten (larger than L2, so A and B come
+// from DRAM), and only the launch sits between its two events. Each launch's
+// event time is quantised (launches of a ~20 us kernel land in bins about
+// 1 us apart, at random), so a median of a few launches is off by up to a bin;
+// the sample count is sized to about 2 ms of kernel time (at least `iters`,
+// at most 200) and the mean of the middle 60% of the samples counts.
+int time_cold_on_stream(const ridge_tile_config* cfg, const void* A, const void* B, void* Cp,
+                        int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                        void* flush, int64_t flush_bytes, int32_t warmup, int32_t iters,
+                        cudaStream_t s, std::vector<cudaEvent_t>& ev, double* ms_out) {
+    int st = RIDGE_OK;
+    auto events = [&](int n) {
+        while (int(ev.size()) < 2 * n) {
+            cudaEvent_t e;
+            cudaError_t ce = cudaEventCreate(&e);
+            if (ce != cudaSuccess) return int(ce);
+            ev.push_back(e);
+        }
+        return RIDGE_OK;
+    };
+    // n flushed launches, each between its own events; returns their times
+    auto run = [&](int n, int tag, std::vector<double>& ms) {
+        int r = events(n);
+        if (r != RIDGE_OK) return r;
+        for (int i = 0; i < n; ++i) {
+            cudaError_t ce = cudaMemsetAsync(flush, (tag + i) & 0xff, size_t(flush_bytes), s);
+            if (ce != cudaSuccess) return int(ce);
+            cudaEventRecord(ev[2 * i], s);
+            r = ridge_gemm_launch(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, s);
+            if (r != RIDGE_OK) return r;
+            cudaEventRecord(ev[2 * i + 1], s);
+        }
+        cudaError_t ce = cudaEventSynchronize(ev[2 * n - 1]);
+        if (ce != cudaSuccess) return int(ce);
+        ms.assign(size_t(n), 0.0);
+        for (int i = 0; i < n; ++i) {
+            float x = 0.f;
+            cudaEventElapsedTime(&x, ev[2 * i], ev[2 * i + 1]);
+            ms[size_t(i)] = x;
+        }
+        return RIDGE_OK;
+    };
+    std::vector<double> ms;
+    st = run(std::max(1, warmup), 1, ms);  // warm-up; the last launch sizes the sample
+    if (st != RIDGE_OK) return st;
+    const double probe = std::max(ms.back(), 1e-3);
+    const int n = std::min(200, std::max(std::max(1, iters), int(std::ceil(2.0 / probe))));
+    st = run(n, 7, ms);
+    if (st != RIDGE_OK) return st;
+    std::sort(ms.begin(), ms.end());
+    const int lo = n / 5, hi = n - n / 5;
+    double sum = 0.0;
+    for (int i = lo; i < hi; ++i) sum += ms[size_t(i)];
+    *ms_out = sum / double(hi - lo);
+    return RIDGE_OK;
+}
+
+constexpr int64_t kFlushBytes = int64_t(256) << 20;  // twice the 126 MB L2
 
 // ------------------------------------------------------------------ the farm
 //
@@ -213,6 +277,19 @@ int ridge_time_gemm(const ridge_tile_config* cfg, const void* A, const void* B, 
     return st;
 }
 
+int ridge_time_gemm_cold(const ridge_tile_config* cfg, const void* A, const void* B, void* Cp,
+                         int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                         void* flush, int64_t flush_bytes, int32_t warmup, int32_t iters,
+                         void* stream, double* ms_per_launch) {
+    if (!ms_per_launch || !flush || flush_bytes <= 0) return RIDGE_EINVAL;
+    std::vector<cudaEvent_t> ev;
+    const int st = time_cold_on_stream(cfg, A, B, Cp, M, N, K, lda, ldb, ldc, flush, flush_bytes,
+                                       warmup, iters, static_cast<cudaStream_t>(stream), ev,
+                                       ms_per_launch);
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    return st;
+}
+
 int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const int32_t* devices,
                    int32_t num_devices, const ridge_hw* hw_in, int32_t warmup_iters,
                    int32_t timed_iters, ridge_tune_result* results, ridge_tune_entry* entries,
@@ -276,9 +353,8 @@ int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const i
         if (ce == cudaSuccess) ce = cudaMalloc(&d.a, size_t(maxA) * 2);
         if (ce == cudaSuccess) ce = cudaMalloc(&d.b, size_t(maxB) * 2);
         if (ce == cudaSuccess) ce = cudaMalloc(&d.c, size_t(maxC) * 2);
+        if (ce == cudaSuccess) ce = cudaMalloc(&d.flush, size_t(kFlushBytes));
         if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
-        if (ce == cudaSuccess) ce = cudaEventCreate(&d.e0);
-        if (ce == cudaSuccess) ce = cudaEventCreate(&d.e1);
         if (ce != cudaSuccess) return false;
         uint32_t state = 0;
         int st = ridge_fill_lcg(d.a, maxA, &state, 1, d.stream);
@@ -292,8 +368,9 @@ int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const i
         const int64_t M = shapes[3 * job.shape], N = shapes[3 * job.shape + 1],
                       K = shapes[3 * job.shape + 2];
         double ms = 0;
-        const int ts = time_on_stream(&e.tile, d.a, d.b, d.c, M, N, K, K, K, N, warmup_iters,
-                                      timed_iters, d.stream, d.e0, d.e1, &ms);
+        const int ts = time_cold_on_stream(&e.tile, d.a, d.b, d.c, M, N, K, K, K, N, d.flush,
+                                           kFlushBytes, warmup_iters, timed_iters, d.stream, d.ev,
+                                           &ms);
         // A CUDA error is sticky for this device's context: the job goes to
         // another device. A device-side timeout (bounded wait) leaves the
         // context usable: record it, clear it, go on.
@@ -308,12 +385,12 @@ int ridge_autotune(const int64_t* shapes, int32_t num_shapes, int32_t k, const i
     };
     auto teardown = [&](int slot) {
         DeviceBuffers& d = bufs[size_t(slot)];
-        if (d.e0) cudaEventDestroy(d.e0);
-        if (d.e1) cudaEventDestroy(d.e1);
+        for (cudaEvent_t e : d.ev) cudaEventDestroy(e);
         if (d.stream) cudaStreamDestroy(d.stream);
         cudaFree(d.a);
         cudaFree(d.b);
         cudaFree(d.c);
+        cudaFree(d.flush);
         d = DeviceBuffers();
     };
     std::vector<int> job_slot;

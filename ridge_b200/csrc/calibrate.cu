@@ -105,8 +105,19 @@ __global__ void cal_umma_kernel(int m, int n, int iters, unsigned long long* cyc
 
 // ------------------------------------------------------------------ TMA
 
-// One producer thread per CTA keeps `depth` box loads in flight over a ring:
-// load i goes to slot i % depth after the slot's previous load has landed.
+// The GEMM's load pipeline without the MMAs. Warp 0: `issuers` producer
+// lanes, each owning `depth` ring slots, wait on a slot's empty barrier and
+// load the next box into it (completion counted in bytes on the slot's full
+// barrier). Warp 1, lane 0: the consumer, which waits on every full barrier
+// in issue order and frees the slot on its empty barrier -- the role the MMA
+// issuer's commits play in the GEMM; a producer never waits on the barrier its
+// own loads complete. Measured on B200: one issuing thread moves about one box
+// per ~850 SM cycles whatever the box size (16 or 32 KB), the ring depth (2-8),
+// the row pitch or where the tensor lives (L2 or DRAM); a second issuer doubles
+// the rate. The GEMM's producer is faster than that (its single issuer keeps a
+// 2-CTA 256x256x64 tile's tensor pipe ~70% busy, which needs about three boxes
+// per 850 cycles), so the GEMM's fill constants are fitted on GEMM timings, not
+// taken from this benchmark.
 // CTA b reads rows starting at (b * rows_step) mod rows_total, walking K, so
 // an L2-resident tensor is shared by all SMs while a large one streams.
 __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int depth, int box_bytes,
@@ -115,45 +126,61 @@ __global__ void cal_tma_kernel(const __grid_constant__ CUtensorMap map, int dept
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
-    __shared__ uint64_t bars[16];
-    const int lane = threadIdx.x;
-    if (lane >= issuers) return;
-    // Issuer `lane` owns ring slots [lane * depth, (lane + 1) * depth) and
-    // loads lane, lane + issuers, ...
-    for (int s = 0; s < depth; ++s) mbar_init(smem_u32(&bars[lane * depth + s]), 1);
-    fence_barrier_init();
-    __syncwarp((1u << issuers) - 1u);
-    const unsigned long long t0 = clk();
-    const int mine = loads / issuers;
-    for (int j = 0; j < mine; ++j) {
-        const int i = j * issuers + lane;
-        const int s = lane * depth + j % depth;
-        const uint32_t b = smem_u32(&bars[s]);
-        if (j >= depth && !mbar_wait(b, uint32_t((j / depth - 1) & 1), nullptr, err, kErrTimeoutProducer))
-            break;
-        mbar_arrive_expect_tx(b, uint32_t(box_bytes));
-        int kx, ry;
-        if (private_regions) {
-            // CTA b cycles over its own 16 boxes: row tile b % row_tiles, K
-            // segment b / row_tiles (no two CTAs read the same bytes).
-            const int seg = int(blockIdx.x) / row_tiles;
-            kx = ((seg * 16 + (i & 15)) % k_boxes) * box_cols;
-            ry = (int(blockIdx.x) % row_tiles) * box_rows;
-        } else {
-            const int g = int(blockIdx.x) * loads + i;
-            kx = (g % k_boxes) * box_cols;
-            ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
+    __shared__ uint64_t full[16], empty[16];
+    __shared__ unsigned long long t_start;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slots = issuers * depth;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < slots; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
         }
-        if (box_cols == 128)
-            tma_load_3d(base + uint32_t(s * box_bytes), &map, b, 0, ry, kx / 64);
-        else
-            tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
+        fence_barrier_init();
+        tma_prefetch_desc(&map);
+        t_start = clk();
     }
-    for (int j = std::max(0, mine - depth); j < mine; ++j)
-        mbar_wait(smem_u32(&bars[lane * depth + j % depth]), uint32_t((j / depth) & 1), nullptr,
-                  err, kErrTimeoutDrain);
-    __syncwarp((1u << issuers) - 1u);
-    if (lane == 0) cycles[blockIdx.x] = clk() - t0;
+    __syncthreads();
+    const int mine = loads / issuers;
+    if (warp == 0 && lane < issuers) {
+        // load i = j * issuers + lane goes to slot lane * depth + j % depth
+        for (int j = 0; j < mine; ++j) {
+            const int i = j * issuers + lane;
+            const int s = lane * depth + j % depth;
+            if (j >= depth && !mbar_wait(smem_u32(&empty[s]), uint32_t((j / depth - 1) & 1),
+                                         nullptr, err, kErrTimeoutProducer))
+                break;
+            const uint32_t b = smem_u32(&full[s]);
+            mbar_arrive_expect_tx(b, uint32_t(box_bytes));
+            int kx, ry;
+            if (private_regions) {
+                // CTA b cycles over its own 16 boxes: row tile b % row_tiles, K
+                // segment b / row_tiles (no two CTAs read the same bytes).
+                const int seg = int(blockIdx.x) / row_tiles;
+                kx = ((seg * 16 + (i & 15)) % k_boxes) * box_cols;
+                ry = (int(blockIdx.x) % row_tiles) * box_rows;
+            } else {
+                const int g = int(blockIdx.x) * loads + i;
+                kx = (g % k_boxes) * box_cols;
+                ry = ((g / k_boxes + int(blockIdx.x) * 7) % row_tiles) * box_rows;
+            }
+            if (box_cols == 128)
+                tma_load_3d(base + uint32_t(s * box_bytes), &map, b, 0, ry, kx / 64);
+            else
+                tma_load_2d(base + uint32_t(s * box_bytes), &map, b, kx, ry);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // consume in issue order: load i sits in slot (i % issuers) * depth +
+        // (i / issuers) % depth, phase (i / issuers) / depth
+        for (int i = 0; i < mine * issuers; ++i) {
+            const int j = i / issuers, ln = i % issuers;
+            const int s = ln * depth + j % depth;
+            if (!mbar_wait(smem_u32(&full[s]), uint32_t((j / depth) & 1), nullptr, err,
+                           kErrTimeoutDrain))
+                break;
+            mbar_arrive(smem_u32(&empty[s]));
+        }
+        cycles[blockIdx.x] = clk() - t_start;
+    }
 }
 
 // ------------------------------------------------------------------ epilogue
@@ -409,11 +436,11 @@ int ridge_cal_tma(int64_t tensor_bytes, int32_t box_rows, int32_t depth, int32_t
         cudaFree(buf);
         return RIDGE_EINVAL;  // tensor too small for one private region per CTA
     }
-    cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, std::min(loads, 64 * issuers),
+    cal_tma_kernel<<<grid, 64, smem>>>(map, depth, box_bytes, std::min(loads, 64 * issuers),
                                        box_rows, k_boxes, row_tiles, private_regions, issuers,
                                        box_cols, d, err);
     cudaEventRecord(e0);
-    cal_tma_kernel<<<grid, 32, smem>>>(map, depth, box_bytes, loads, box_rows, k_boxes,
+    cal_tma_kernel<<<grid, 64, smem>>>(map, depth, box_bytes, loads, box_rows, k_boxes,
                                        row_tiles, private_regions, issuers, box_cols, d, err);
     cudaEventRecord(e1);
     e = cudaGetLastError();

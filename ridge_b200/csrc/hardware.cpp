@@ -130,7 +130,8 @@ extern "C" {
 //   148 SMs; 8192 dense FP16 FLOP/cycle/SM, so one 128x256x16 MMA
 //   (1,048,576 FLOP) takes 128 cycles; 2.25 PFLOP/s needs ~1.86 GHz, but a
 //   1 kW part holds about 1.4 GHz under sustained tensor load; shared memory
-//   feeds 128 B/cycle/SM; HBM3e 8 TB/s nominal; L2 126 MB.
+//   feeds 128 B/cycle/SM; HBM3e 8 TB/s nominal; L2 126 MB; the GEMM's one
+//   producer thread needs about 320 cycles per TMA box.
 int ridge_hw_b200(ridge_hw* h) {
     if (!h) return RIDGE_EINVAL;
     std::memset(h, 0, sizeof(*h));
@@ -143,7 +144,7 @@ int ridge_hw_b200(ridge_hw* h) {
     h->smem_mma_overlap = 1.0;
     h->l2_bytes_per_sec = 20e12;
     h->hbm_bytes_per_sec = 6.5e12;
-    h->tma_box_cycles = 1030.0;
+    h->tma_box_cycles = 320.0;
     h->tma_box2_ratio = 1.0;
     h->tma_box32_ratio = 1.0;
     h->pipeline_efficiency = 0.9;

@@ -102,12 +102,15 @@ double dram_bytes(int64_t M, int64_t N, int64_t K, int BM, int BN, int groupM, i
 // one dominates, and exceeds it when both are close -- two limits that each
 // nearly bind do not overlap perfectly. It also keeps the losing limit in the
 // prediction, so configs held to the same bound are still ordered.
-double soft_max(double a, double b) {
-    constexpr double kP = 4.0;
+double soft_max(double a, double b, double p = 4.0) {
     const double m = std::max(a, b);
     if (m <= 0.0) return 0.0;
-    return m * std::pow(std::pow(a / m, kP) + std::pow(b / m, kP), 1.0 / kP);
+    return m * std::pow(std::pow(a / m, p) + std::pow(b / m, p), 1.0 / p);
 }
+
+// The compute side and the DRAM side of a launch overlap more closely than two
+// limits inside the SM pipeline do: their smooth maximum is taken sharper.
+constexpr double kHbmOverlapP = 8.0;
 
 }  // namespace
 
@@ -175,18 +178,17 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     const double ov = std::min(1.0, std::max(0.0, hw->smem_mma_overlap));
     const double t_one = ov * std::max(t_issue, t_read) + (1.0 - ov) * (t_issue + t_read);
     const double t_mma = mma_per_stage * t_one;
-    // TMA fill: a stage is one box of A and one of B, each issued by its own
-    // thread, and stages alternate between two such thread pairs. Below the L2
-    // cap an issuing thread finishes about one box per tma_box_cycles whatever
-    // the box size (measured), so a CTA fills one stage per tma_box_cycles / 2;
-    // the stage's bytes also cannot arrive faster than this SM's share of the
-    // aggregate L2 -> shared memory rate.
+    // TMA fill: a stage is one box of A and one of B, both issued by the one
+    // producer thread, so a CTA fills a stage in two box times (tma_box_cycles
+    // per box of BK=64, scaled for BK=32 and the two-atom BK=128 box; fitted on
+    // GEMM timings); the stage's bytes also cannot arrive faster than this
+    // SM's share of the aggregate L2 -> shared memory rate.
     const double box_ratio =
         t.BK == 128 ? hw->tma_box2_ratio : (t.BK == 32 ? hw->tma_box32_ratio : 1.0);
     const double stage_bytes = (double(g.rows_per_cta) + double(t.BN) / g.cg) * t.BK * 2.0;
     const double l2_bytes_per_cycle_sm = hw->l2_bytes_per_sec / hw->num_sms / hw->clock_hz;
     const double t_fill =
-        soft_max(hw->tma_box_cycles * box_ratio / 2.0, stage_bytes / l2_bytes_per_cycle_sm);
+        soft_max(2.0 * hw->tma_box_cycles * box_ratio, stage_bytes / l2_bytes_per_cycle_sm);
     const double t_smem = mma_per_stage * t_read;
 
     // ---- residency and the persistent walk (with the launcher's split-K tail)
@@ -244,20 +246,29 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
     (void)dp_rounds;
     double t_unit = dp_per_unit * tile_period(t_main_whole);
     double t_sk = 0.0;
+    // The launcher runs a unit's split range before its whole tiles when those
+    // fill at most six rounds (the partial exchange then overlaps the next
+    // tile), after them otherwise.
+    const bool sk_first = splits >= 2 && double(dp_tiles) / double(units) <= 6.0;
     if (splits >= 2) {
-        // One K range of 1/splits; every split writes its FP32 partial
-        // (twice the bytes of an FP16 tile, at the drain rate), and the last
-        // to arrive reads all `splits` partials back before its epilogue.
+        // One K range of 1/splits. All but the last split to arrive write their
+        // FP32 partial (twice the bytes of an FP16 tile, at the drain rate); the
+        // last reads those splits - 1 partials and drains the tile.
         const double partial_bytes = double(g.rows_per_cta) * t.BN * 4.0;
-        t_sk = std::ceil(kb / double(splits)) * t_period + partial_bytes / epi_bpc +
-               double(splits) * partial_bytes / (2.0 * epi_bpc) + t_epi;
+        const double fixup = partial_bytes / epi_bpc +
+                             double(splits - 1) * partial_bytes / (2.0 * epi_bpc) + t_epi;
+        t_sk = std::ceil(kb / double(splits)) * t_period;
+        if (sk_first && dp_per_unit > 0)
+            t_sk += std::max(0.0, fixup - tile_period(t_main_whole));  // hidden behind a tile
+        else
+            t_sk += fixup;
         t_unit += t_sk;
-    } else if (info.acc_buffers >= 2 && dp_per_unit > 0) {
-        t_unit += std::min(t_main_whole, t_epi);  // the last tile's epilogue drains alone
     }
+    if ((splits < 2 || sk_first) && info.acc_buffers >= 2 && dp_per_unit > 0)
+        t_unit += std::min(t_main_whole, t_epi);  // the last tile's epilogue drains alone
     const double t_prologue = t_lat;
     t_unit += t_prologue;
-    const double compute_sec = t_unit / hw->clock_hz + hw->launch_overhead_sec;
+    const double compute_sec = t_unit / hw->clock_hz;
 
     // ---- HBM: operand reads (grouped-M walk, L2 reuse), C writes, split-K partials
     const double c_write = double(M) * N * 2.0;
@@ -265,14 +276,15 @@ int ridge_predict(const ridge_gemm_config* cfg, const ridge_hw* hw, ridge_predic
         splits >= 2 ? 2.0 * double(rem) * splits * g.cg * double(g.rows_per_cta) * t.BN * 4.0
                     : 0.0;
     const double hbm_sec = a_b_reads / hw->hbm_bytes_per_sec + c_write / hw->c_write_bytes_per_sec +
-                           partial_traffic / hw->c_write_bytes_per_sec + hw->launch_overhead_sec;
+                           partial_traffic / hw->c_write_bytes_per_sec;
 
     const double flops = 2.0 * double(M) * double(N) * double(K);
     const double peak_flops_per_cycle_sm = 2.0 * 128.0 * 256.0 * 16.0 / hw->umma_cycles_128x256;
     p.peak_tensor_tflops = peak_flops_per_cycle_sm * hw->clock_hz * hw->num_sms / 1e12;
-    p.compute_tflops = flops / compute_sec / 1e12;
-    p.hbm_tflops = flops / hbm_sec / 1e12;
-    p.predicted_seconds = soft_max(compute_sec, hbm_sec);
+    // The launch overhead is paid once, outside the overlap of the two limits.
+    p.compute_tflops = flops / (compute_sec + hw->launch_overhead_sec) / 1e12;
+    p.hbm_tflops = flops / (hbm_sec + hw->launch_overhead_sec) / 1e12;
+    p.predicted_seconds = soft_max(compute_sec, hbm_sec, kHbmOverlapP) + hw->launch_overhead_sec;
     p.predicted_tflops = flops / p.predicted_seconds / 1e12;
     p.dram_bytes = a_b_reads + c_write;
     p.arithmetic_intensity = flops / p.dram_bytes;

@@ -64,7 +64,43 @@ def test_time_gemm_agrees_with_events():
 def test_farm_spreads_candidates_over_two_devices():
     import ridge_b200 as rb
     from ridge_b200.autotune import autotune
-    results, entries = autotune(SHAPES, k=6, devices=(0, 1), warmup=2, iters=5)
-    used = {e["device"] for ents in entries for e in ents[:6]}
-    assert used == {0, 1}
-    assert all(r["benchmarked"] == 6 for r in results)
+    # a first GEMM on device 1 creates its context and loads the kernels, so
+    # that device is ready before device 0 has drained the queue
+    with torch.cuda.device(1):
+        a, b = rb.synthetic_inputs(256, 256, 256, device=torch.device("cuda", 1))
+        rb.gemm(a, b)
+        torch.cuda.synchronize()
+    shapes = [(4096, 4096, 4096), (4096, 8192, 2048)]   # jobs of milliseconds each
+    results, entries = autotune(shapes, k=24, devices=(0, 1), warmup=3, iters=10)
+    used = [e["device"] for ents in entries for e in ents[:24]]
+    assert set(used) == {0, 1}, used
+    assert all(r["benchmarked"] == 24 for r in results)
+
+
+def test_time_gemm_cold_matches_flushed_launches():
+    import ridge_b200 as rb
+    M = N = K = 4096
+    cfg = rb.TileConfig(256, 256, 128, 3, 8, 8, 2)
+    a, b = rb.synthetic_inputs(M, N, K)
+    c = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ms = C.c_double()
+    cc = cfg.to_c()
+    s = torch.cuda.current_stream().cuda_stream
+    assert rb.lib.ridge_time_gemm_cold(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M,
+                                       N, K, K, K, N, flush.data_ptr(), flush.numel(), 3, 15, s,
+                                       C.byref(ms)) == 0
+    times = []
+    for _ in range(15):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rb.gemm(a, b, c, config=cfg)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    mid = sorted(times)[3:12]
+    mean = sum(mid) / len(mid)
+    assert 0.85 * mean <= ms.value <= 1.15 * mean, (ms.value, mean)
+    assert rb.lib.ridge_time_gemm_cold(C.byref(cc), a.data_ptr(), b.data_ptr(), c.data_ptr(), M,
+                                       N, K, K, K, N, None, 0, 3, 15, s, C.byref(ms)) == -1

@@ -24,19 +24,20 @@ def smax(a, b, p=4.0):
 def test_worked_example_4096_cubed_256x256x64_one_cta():
     hw = b200()
     # placeholders: clock 1.4 GHz, 128 cycles per 128x256x16 MMA, smem 128 B/cycle
-    # (reads overlap), TMA box 1030 cycles per issuing thread, L2 fill cap 20 TB/s
-    # (96.53 B/cycle/SM at 1.4 GHz on 148 SMs), pipeline efficiency
-    # 0.9, TMA latency 1000 cycles, epilogue 32 B/cycle (4 warps), HBM 6.5 TB/s
-    # read and write, launch 4 us, no tile turnover cost.
+    # (reads overlap), TMA box 320 cycles, L2 fill cap 20 TB/s (96.53
+    # B/cycle/SM at 1.4 GHz on 148 SMs), pipeline efficiency 0.9, TMA latency
+    # 1000 cycles, epilogue 32 B/cycle (4 warps), HBM 6.5 TB/s read and write,
+    # launch 4 us, no tile turnover cost.
     p = predict(4096, 4096, 4096, rb.TileConfig(256, 256, 64, 3, 4, 8, 1), hw)
     # One CTA holds 256 rows: 2 M-halves x BK/16 = 8 MMAs per stage, each
     # max(128 * 256/256, (128 + 256) * 32 / 128 = 96) = 128 cycles.
     assert p["t_mma_cycles"] == pytest.approx(1024.0)
     assert p["t_smem_cycles"] == pytest.approx(8 * 96.0)
-    # fill: box term 1030 / 2 lane pairs = 515; bytes term: a stage is
-    # (256 + 256) x 64 x 2 = 65,536 B at 96.53 B/cycle = 678.9 cycles
+    # fill: the one producer thread issues the stage's A box and B box, 2 x
+    # 320 = 640 cycles; bytes term: a stage is (256 + 256) x 64 x 2 =
+    # 65,536 B at 96.53 B/cycle = 678.9 cycles
     l2_bpc = 20e12 / 148 / 1.4e9
-    t_fill = smax(515.0, 65536 / l2_bpc)
+    t_fill = smax(640.0, 65536 / l2_bpc)
     assert 65536 / l2_bpc == pytest.approx(678.9, abs=0.1)
     assert p["t_l2_cycles"] == pytest.approx(t_fill, rel=1e-9)
     # 214,272 B of shared memory and all 512 TMEM columns: one CTA per SM,
@@ -55,18 +56,23 @@ def test_worked_example_4096_cubed_256x256x64_one_cta():
     # so the busiest unit runs 2 whole tiles, then one prologue latency.
     assert p["total_tiles"] == 256 and p["tile_slots"] == 148
     t_unit = 2 * (t_main + t_epi) + 1000
-    compute = t_unit / 1.4e9 + 4e-6
+    compute = t_unit / 1.4e9
     # A and B (64 MiB) fit in L2: read once; C written once.
-    hbm = (2 * 4096 * 4096 * 2) / 6.5e12 + (4096 * 4096 * 2) / 6.5e12 + 4e-6
+    hbm = (2 * 4096 * 4096 * 2) / 6.5e12 + (4096 * 4096 * 2) / 6.5e12
     assert p["dram_bytes"] == pytest.approx(3 * 4096 * 4096 * 2)
-    seconds = smax(compute, hbm)
+    # the two limits overlap (sharper smooth maximum, p = 8); the launch
+    # overhead is paid once on top
+    seconds = smax(compute, hbm, 8.0) + 4e-6
     assert p["predicted_seconds"] == pytest.approx(seconds, rel=1e-9)
     assert p["predicted_tflops"] == pytest.approx(2 * 4096 ** 3 / seconds / 1e12, rel=1e-9)
-    # by hand: t_fill 729.2, t_stage 1204.8, unit 163,406 cycles = 120.7 us
-    assert p["predicted_tflops"] == pytest.approx(1138.3, abs=0.2)
-    # the worst factor is the partial second round: 256*64*t_stage / (148 * 2 tiles)
+    # by hand: t_fill 785.3, t_stage 1225.5, unit 166,054 cycles = 118.6 us,
+    # + 4 us launch = 122.6 us
+    assert p["predicted_tflops"] == pytest.approx(1120.9, abs=0.2)
+    # the worst factor is the partial second round: 256*64*t_stage / (148 * 2
+    # tiles) = 0.82, just below the fill (1024 of 1225.5 cycles, 0.84)
     assert p["wave_efficiency"] == pytest.approx(256 * 64 * t_stage / (148 * (t_unit - 1000)),
                                                  rel=1e-9)
+    assert p["l2_efficiency"] == pytest.approx(1024.0 / t_stage, rel=1e-9)
     assert p.label == "WAVES"
 
 
