@@ -25,7 +25,8 @@ c5      = BASELINE config 5 beside the headline: 16384^3 split into N-column
           every rank's full C over NVLink (ridge_gemm_sharded_p2p), timed as max
           over ranks, with the NCCL all-gather variant (ridge_gemm_sharded) and
           the GEMM alone beside it, and the gathered C checked on every rank
-          against an FP64 product of sampled rows.
+          against an FP64 product of sampled rows; the tile is the autotuner's
+          pick for the slab shape (top 10 of the model, measured on rank 0).
 --impl reference  times the reference's own CPU GEMM (referenceGemm, FP64,
           bench/check-gemm.cu:98-108, built from the reference sources into
           oracle/_ref) on all host cores over a row sample of the same workload.
@@ -300,7 +301,28 @@ def _fp16_check(got, ref):
     return rel, float((d - half_ulp).max())
 
 
-def c5_record(cfg, world, rank, dev, steps=3, rounds=3, warmup=1):
+def c5_tile(world, rank, dev, M, ns, K):
+    """The autotuned tile for one rank's slab shape (BASELINE config 5 uses "the
+    autotuned best config per slab shape"): rank 0 runs the model-pruned
+    autotuner (top 10 measured, L2-flushed) on its GPU and every rank takes its
+    pick, so all ranks run the same tile."""
+    import torch
+    import torch.distributed as dist
+
+    import ridge_b200 as rb
+    from ridge_b200.autotune import autotune
+    vals = torch.zeros(8, dtype=torch.int64, device=dev)
+    if rank == 0:
+        res, _ = autotune([(M, ns, K)], k=10, devices=(dev.index,), warmup=2, iters=5)
+        t = res[0]["best"]
+        vals = torch.tensor([t.BM, t.BN, t.BK, t.stages, t.warps, t.groupM, t.cta_group,
+                             t.split_k], dtype=torch.int64, device=dev)
+    if world > 1:
+        dist.broadcast(vals, 0)
+    return rb.TileConfig(*[int(v) for v in vals.tolist()])
+
+
+def c5_record(world, rank, dev, steps=3, rounds=3, warmup=1):
     """BASELINE config 5 on `world` ranks: 16384^3 split into N-column slabs of
     B with A replicated, C gathered on every rank. Returns the sub-record."""
     import torch
@@ -311,6 +333,7 @@ def c5_record(cfg, world, rank, dev, steps=3, rounds=3, warmup=1):
 
     M = N = K = C5_SHAPE
     n0, ns = slab_bounds(N, world, rank)
+    cfg = c5_tile(world, rank, dev, M, ns, K)
     a = torch.empty((M, K), dtype=torch.float16, device=dev)
     st_b = rb.fill_lcg(a, 0)
     b_slab = torch.empty((max(ns, 1), K), dtype=torch.float16, device=dev)[:ns]
@@ -397,7 +420,8 @@ def c5_record(cfg, world, rank, dev, steps=3, rounds=3, warmup=1):
     rec = {
         "workload": "%dx%dx%d FP16 GEMM in %d N-slab(s) of %d columns, A replicated, full C "
                     "gathered on every rank" % (M, N, K, world, ns),
-        "tile": cfg.as_dict(), "launches_per_variant": steps * rounds, "warmup": warmup,
+        "tile": cfg.as_dict(), "tile_source": "ridge_autotune top 10 for the slab shape, rank 0",
+        "launches_per_variant": steps * rounds, "warmup": warmup,
         "ms_fused_gather": fused_ms, "tflops_fused_gather": flops / (fused_ms * 1e-3) / 1e12,
         "frac_of_n_peak": flops / (fused_ms * 1e-3) / 1e12 / (world * peak),
         "peak_source": peak_src + " bf16 dense (burst), per GPU",
@@ -546,7 +570,7 @@ def run_ridge(args):
 
     c5 = None
     if not args.no_c5:
-        c5 = c5_record(cfg, world, rank, dev)
+        c5 = c5_record(world, rank, dev)
 
     # ------------------------------------------------ report (rank 0)
     if rank == 0:

@@ -145,3 +145,19 @@ def test_gemm_sharded_validates_before_touching_the_gpu():
     assert lib.ridge_gemm_sharded(*args(0, 0, 0, None)) == RIDGE_EINVAL     # no ranks
     assert lib.ridge_gemm_sharded(*args(2, 0, 1, None)) == RIDGE_EINVAL     # gather, no comm
     assert lib.ridge_status_string(-7).decode().startswith("NCCL")
+
+
+def test_lcg_advance_matches_drawing_the_stream():
+    """ridge_b200.lcg_advance(state, n) is the state after n draws, so a rank can
+    start its slab of B without generating the rows before it."""
+    import ctypes as C
+    import numpy as np
+
+    import oracle
+    import ridge_b200 as rb
+    for seed, n in [(0, 0), (0, 1), (5, 1000), (123456789, 4097)]:
+        st = C.c_uint32(seed)
+        buf = np.empty(max(n, 1), np.uint16)
+        if n:
+            oracle.lib.oracle_fill_unit(buf.ctypes.data_as(C.c_void_p), n, C.byref(st))
+        assert rb.lcg_advance(seed, n) == st.value
