@@ -188,17 +188,6 @@ int tma_issuers() {
     return n;
 }
 
-// How the fused-gather epilogue writes the peer copies of C: 1 = from the
-// epilogue warps' registers with global stores, 0 = TMA stores from the
-// staging buffer. Read once from RIDGE_PEER_DIRECT (a knob for measurement).
-int peer_direct_stores() {
-    static const int n = [] {
-        const char* v = std::getenv("RIDGE_PEER_DIRECT");
-        return v ? (std::atoi(v) != 0 ? 1 : 0) : 0;
-    }();
-    return n;
-}
-
 // BM=256 tiles default to the 2-CTA pair (half the shared-memory operand
 // traffic per SM and two TMEM accumulators); cta_group 1 selects the
 // single-CTA form explicitly.
@@ -544,9 +533,6 @@ int launch_common(const ridge_tile_config* cfg, const void* A, const void* B, vo
     p.epi_stride = plan.epi_stride;
     p.tma_issuers = tma_issuers();
     p.num_peers = num_peers;
-    p.peer_direct = num_peers > 0 ? peer_direct_stores() : 0;
-    for (int d = 0; d < kMaxPeers; ++d)
-        p.peer_c[d] = d < num_peers ? static_cast<__half*>(peer_c[d]) : nullptr;
     p.err = dev->err_word;
     p.dp_tiles = plan.dp_tiles;
     p.sk_tiles = plan.sk_tiles;

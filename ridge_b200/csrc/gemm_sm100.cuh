@@ -130,12 +130,6 @@ struct GemmParams {
     int epi_stride; // staging bytes per epilogue warp: 4096, or 8192 for two pair buffers
     int tma_issuers; // producer threads issuing TMA loads: 1, 2 or 4
     int num_peers;  // destinations in PeerMaps besides tmap_c (TMA-store epilogue only)
-    // peer_direct = 1: the epilogue warps write the peer copies of each chunk
-    // straight from registers (16-byte global stores to peer_c[d], the same
-    // addresses the peer maps cover), and only this GPU's C goes through TMA;
-    // 0: every copy is a TMA store from the staging buffer.
-    int peer_direct;
-    __half* peer_c[kMaxPeers];
     int* err;
     // Split-K tail ("data-parallel + stream-K"): tiles [0, dp_tiles) run whole,
     // one per unit per round; the remaining sk_tiles tiles are each split into
@@ -595,40 +589,6 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                     add_into_r(q);
                 }
             };
-            // Peer copies written from registers: lane L holds row warp_row0 + L
-            // of the chunk, `cols` (32 or 64) FP16 columns from col0 -- the
-            // first 32 in `lo`, the next 32 in `hi`. Each lane writes its row
-            // with 16-byte stores to every peer's C (peer rows are 16-byte
-            // aligned: pitch and base checked by the launcher).
-            auto store_peers = [&](int warp_row0, int col0, const uint32_t (&lo)[16],
-                                   const uint32_t (&hi)[16], int cols) {
-                const long long row = (long long)tile_row0 + warp_row0 + lane;
-                if ((BM == 64 && lane >= 16) || row >= p.M) return;
-#pragma unroll 1
-                for (int d = 0; d < p.num_peers; ++d) {
-                    __half* crow = p.peer_c[d] + row * p.ldc;
-                    if (col0 + cols <= p.N) {
-                        uint4* dst = reinterpret_cast<uint4*>(crow + col0);
-#pragma unroll
-                        for (int v = 0; v < 4; ++v)
-                            dst[v] = make_uint4(lo[4 * v], lo[4 * v + 1], lo[4 * v + 2],
-                                                lo[4 * v + 3]);
-                        if (cols == 64) {
-#pragma unroll
-                            for (int v = 0; v < 4; ++v)
-                                dst[4 + v] = make_uint4(hi[4 * v], hi[4 * v + 1], hi[4 * v + 2],
-                                                        hi[4 * v + 3]);
-                        }
-                    } else {
-                        for (int e = 0; e < cols && col0 + e < p.N; ++e) {
-                            const uint32_t word = e < 32 ? lo[(e >> 1) & 15] : hi[((e - 32) >> 1) & 15];
-                            const unsigned short bits = (e & 1) ? (unsigned short)(word >> 16)
-                                                                : (unsigned short)(word & 0xffff);
-                            crow[col0 + e] = __ushort_as_half(bits);
-                        }
-                    }
-                }
-            };
             auto store_chunk = [&](int ci, const uint32_t (&packed)[16]) {
                 const int j = group * kPerHalf + ci % kPerHalf;
                 const int warp_row0 = warp_row0_of(ci);
@@ -657,14 +617,11 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                     __syncwarp();
                     if (lane == buf) {
                         tma_store_2d(&tmap_c, sbuf, col0, tile_row0 + warp_row0);
-                        if (!p.peer_direct) {
 #pragma unroll 1
-                            for (int d = 0; d < p.num_peers; ++d)
-                                tma_store_2d(&peers.map[d], sbuf, col0, tile_row0 + warp_row0);
-                        }
+                        for (int d = 0; d < p.num_peers; ++d)
+                            tma_store_2d(&peers.map[d], sbuf, col0, tile_row0 + warp_row0);
                         tma_store_commit();
                     }
-                    if (p.peer_direct) store_peers(warp_row0, col0, packed, packed, 32);
                     buf ^= 1;
                     return;
                 }
@@ -726,13 +683,12 @@ __global__ void __launch_bounds__((2 + WARPS) * 32, 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane <= (p.peer_direct ? 0 : p.num_peers)) {
+                if (lane <= p.num_peers) {
                     tma_store_2d(lane == 0 ? static_cast<const void*>(&tmap_c)
                                            : static_cast<const void*>(&peers.map[lane - 1]),
                                  sbuf, col0, tile_row0 + warp_row0_of(ci));
                     tma_store_commit();
                 }
-                if (p.peer_direct) store_peers(warp_row0_of(ci), col0, pa, pb, 64);
                 ++pidx;
             };
             uint32_t ra[32], rb[32];
