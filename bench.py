@@ -322,7 +322,7 @@ def c5_tile(world, rank, dev, M, ns, K):
     return rb.TileConfig(*[int(v) for v in vals.tolist()])
 
 
-def c5_record(world, rank, dev, steps=3, rounds=3, warmup=1):
+def c5_record(world, rank, dev, steps=3, rounds=3, warmup=1, forced=None):
     """BASELINE config 5 on `world` ranks: 16384^3 split into N-column slabs of
     B with A replicated, C gathered on every rank. Returns the sub-record."""
     import torch
@@ -333,7 +333,7 @@ def c5_record(world, rank, dev, steps=3, rounds=3, warmup=1):
 
     M = N = K = C5_SHAPE
     n0, ns = slab_bounds(N, world, rank)
-    cfg = c5_tile(world, rank, dev, M, ns, K)
+    cfg = forced if forced is not None else c5_tile(world, rank, dev, M, ns, K)
     a = torch.empty((M, K), dtype=torch.float16, device=dev)
     st_b = rb.fill_lcg(a, 0)
     b_slab = torch.empty((max(ns, 1), K), dtype=torch.float16, device=dev)[:ns]
@@ -420,7 +420,9 @@ def c5_record(world, rank, dev, steps=3, rounds=3, warmup=1):
     rec = {
         "workload": "%dx%dx%d FP16 GEMM in %d N-slab(s) of %d columns, A replicated, full C "
                     "gathered on every rank" % (M, N, K, world, ns),
-        "tile": cfg.as_dict(), "tile_source": "ridge_autotune top 10 for the slab shape, rank 0",
+        "tile": cfg.as_dict(),
+        "tile_source": ("given (--c5-config)" if forced is not None else
+                        "ridge_autotune top 10 for the slab shape, rank 0"),
         "launches_per_variant": steps * rounds, "warmup": warmup,
         "ms_fused_gather": fused_ms, "tflops_fused_gather": flops / (fused_ms * 1e-3) / 1e12,
         "frac_of_n_peak": flops / (fused_ms * 1e-3) / 1e12 / (world * peak),
@@ -570,7 +572,9 @@ def run_ridge(args):
 
     c5 = None
     if not args.no_c5:
-        c5 = c5_record(world, rank, dev)
+        forced = (rb.TileConfig(*[int(x) for x in args.c5_config.split(",")])
+                  if args.c5_config else None)
+        c5 = c5_record(world, rank, dev, forced=forced)
 
     # ------------------------------------------------ report (rank 0)
     if rank == 0:
@@ -638,6 +642,9 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ridge", "reference"], default="ridge")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c5", action="store_true", help="skip the 16384^3 sharded sub-record")
+    ap.add_argument("--c5-config", default=None,
+                    help="BM,BN,BK,stages,warps,groupM,cta_group for the sub-record instead of "
+                         "the autotuner's pick")
     ap.add_argument("--panels", type=int, default=0,
                     help="M-panels of the end-to-end host-buffer call (0 = its default)")
     ap.add_argument("--config", default=None,
